@@ -1,0 +1,92 @@
+/*
+ * llmdiy_kernels.h — C ABI of the sm_100a kernels (libllmdiy_b200.so) that
+ * replace the reference's kernel launches one for one.
+ *
+ * Each launcher keeps the parameter list (names, order, meaning) of the
+ * reference kernel or host helper it replaces, cited below as
+ * file:line in SeaTheDestiny/LLM-inference-DIY, and adds:
+ *   - a trailing `stream` (NULL = the legacy default stream the reference uses);
+ *   - an int return: the cudaError_t of the launch (0 = success), instead of
+ *     the reference's silent void launch + later cudaGetLastError.
+ * Buffers are device pointers to IEEE fp16 bit patterns (uint16_t) or fp32;
+ * no launcher allocates, except llmdiy_transpose_weight_gpu, which keeps
+ * the reference helper's allocate / transpose / free / swap contract.
+ * Launch shapes are the launchers' own choice (B200: 148 SMs).
+ */
+#ifndef LLMDIY_KERNELS_H
+#define LLMDIY_KERNELS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* kernels/rmsnorm.cuh:6 rmsnorm_kernel(out, in, weight, d, epsilon), launched <<<1,512>>>
+ * (framework_src/qwen_infer.cu:626). Same reduction tree, bit-identical output. d >= 512. */
+int llmdiy_rmsnorm(uint16_t* out, const uint16_t* in, const uint16_t* weight, int d, float eps, void* stream);
+
+/* kernels/bias.cuh:6 add_bias_kernel(out, bias, size): out = half(out + bias)
+ * (qwen_infer.cu:631 QKV bias, :704 and :721 residual adds). */
+int llmdiy_add_bias(uint16_t* out, const uint16_t* bias, int size, void* stream);
+
+/* kernels/swiglu.cuh:6 swiglu_kernel(out, w1_out, w2_out, size): out = w1 * silu(w2) (qwen_infer.cu:715). */
+int llmdiy_swiglu(uint16_t* out, const uint16_t* w1o, const uint16_t* w2o, int size, void* stream);
+
+/* kernels/fused_qkv_rope_cache.cuh:6 fused_qkv_rope_cache_kernel(d_qkv, d_kv_cache_k, d_kv_cache_v,
+ * pos, max_seqlen, num_heads, head_dim), launched <<<num_heads,64>>> (qwen_infer.cu:634-642). */
+int llmdiy_fused_qkv_rope_cache(uint16_t* qkv, uint16_t* kc, uint16_t* vc, int pos, int max_seqlen, int num_heads,
+                                int head_dim, void* stream);
+
+/* kernels/flash_decode_q1_opt.cuh:434 fd_v5_fused_kernel<128,8,32>(Q, K, V, O_final, KV_seqlen, stride),
+ * <<<1,256>>> per head (qwen_infer.cu:666-668).  Like the reference it attends rows [0, min(L,256)). */
+int llmdiy_fd_v5_fused(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int L, int stride,
+                       void* stream);
+
+/* kernels/flash_decode_q1_opt.cuh:548 fd_v5_split_stage1_kernel<128,256,8>(Q, K, V, O_partial, LSE,
+ * KV_seqlen, num_chunks, stride), <<<num_chunks,256>>> (qwen_infer.cu:671-673). */
+int llmdiy_fd_v5_split_stage1(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* Opart, float* LSE,
+                              int L, int num_chunks, int stride, void* stream);
+
+/* kernels/flash_decode_q1_opt.cuh:666 fd_opt_stage2_kernel<128>(O_partial, LSE, O_final, num_chunks),
+ * <<<1,128>>> (qwen_infer.cu:674-676). */
+int llmdiy_fd_opt_stage2(const uint16_t* Opart, const float* LSE, uint16_t* O, int num_chunks, void* stream);
+
+/* kernels/argmax.cuh:7 argmax_kernel(out_token, logits, vocab_size), <<<1,512>>> (qwen_infer.cu:731).
+ * Reproduces the reference winner among tied maxima; -1 when no value is > -inf. */
+int llmdiy_argmax(int* out, const uint16_t* logits, int V, void* stream);
+
+/* kernels/hgemm_final.cuh:274 hgemv_kernel(A, B, C, N, K): C[n] = sum_k A[k] * B[k*N+n],
+ * B in the reference's transposed [K,N] layout (qwen_infer.cu:359-363). */
+int llmdiy_hgemv(const uint16_t* A, const uint16_t* B, uint16_t* C, int N, int K, void* stream);
+
+/* kernels/hgemm_mma_swizzle.cuh:414 hgemm_swizzle_nn(A, B, C, M, N, K): row-major C[M,N] = A[M,K] * B[K,N]
+ * (qwen_infer.cu:364-366).  Accumulates in fp32 (the reference accumulates in fp16). */
+int llmdiy_hgemm_swizzle_nn(uint16_t* A, uint16_t* B, uint16_t* C, int M, int N, int K, void* stream);
+
+/* kernels/flash_attn.cu:1854 flash_attn_tuned_A_kernel<128,...>(Q, K, V, O, QKV_seqlen, QKV_head,
+ * stride_Q, stride_KV, K_ofs_override, V_ofs_override, Q_ofs_override, O_ofs_override) with the causal
+ * mask the engine compiles in (FLASH_ATTN_CAUSAL, qwen_infer.cu:62, launched per head at :501-516).
+ * Offsets < 0 mean "derive from QKV_head" exactly as the reference does. */
+int llmdiy_flash_attn_tuned_A(uint16_t* Q, uint16_t* K, uint16_t* V, uint16_t* O, int N, int QKV_head,
+                              int stride_Q, int stride_KV, int K_ofs, int V_ofs, int Q_ofs, int O_ofs, void* stream);
+
+/* kernels/gather_qkv.cuh:63 gather_q_from_qkv(d_qkv, d_buf, N, numHeads, kHeadDim, stream) */
+int llmdiy_gather_q_from_qkv(const uint16_t* qkv, uint16_t* buf, int N, int num_heads, int head_dim, void* stream);
+/* kernels/gather_qkv.cuh:75 gather_kv_from_cache(d_cache, d_buf, N, numHeads, kHeadDim, stream) */
+int llmdiy_gather_kv_from_cache(const uint16_t* cache, uint16_t* buf, int N, int num_heads, int head_dim,
+                                void* stream);
+/* kernels/gather_qkv.cuh:39 scatter_interleaved_kernel<128,256>(src, dst, N, numHeads, dst_stride_cols)
+ * (qwen_infer.cu:527-528) */
+int llmdiy_scatter_interleaved(const uint16_t* src, uint16_t* dst, int N, int num_heads, int dst_cols, void* stream);
+
+/* kernels/transpose.cuh:6 transpose_weight_kernel(out, in, rows, cols): out[c*rows+r] = in[r*cols+c] */
+int llmdiy_transpose_weight(uint16_t* out, const uint16_t* in, int rows, int cols, void* stream);
+/* kernels/transpose.cuh:17 transpose_weight_gpu(half*& w, rows, cols): allocates, transposes, frees the
+ * old buffer and replaces *w (qwen_infer.cu:233-242). Synchronous. */
+int llmdiy_transpose_weight_gpu(uint16_t** w, int rows, int cols);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

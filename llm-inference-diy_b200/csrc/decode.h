@@ -1,0 +1,73 @@
+// decode.h — host/device contract of the persistent decode kernel.
+//
+// Device weight layout (chosen by this engine; the .bin file keeps the
+// reference's [out,in] = [N,K] row-major layout, model_weights/convert_weights.py:107-185):
+//   * every GEMV weight stays [N,K] (output rows contiguous along K), so a
+//     group of consecutive rows is one contiguous byte range that a single
+//     bulk copy moves into shared memory;
+//   * qkv_w rows are permuted so that RoPE partners sit next to each other:
+//     unit u of section s (0=q,1=k,2=v), head h, t<64 holds rows
+//     (s*H + h*128 + t, s*H + h*128 + 64 + t);
+//   * ffn_w1 / ffn_w2 are interleaved row by row (w12 row 2n = w1 row n,
+//     row 2n+1 = w2 row n), so one unit carries both SwiGLU operands.
+// Every phase therefore works on "units" of two rows.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace llmdiy {
+
+constexpr int kHidden = 2048;       // hidden size the fused kernel is specialised for
+constexpr int kHeadDim = 128;
+constexpr int kHeads = kHidden / kHeadDim;
+constexpr int kRingStages = 8;       // == consumer warps: slot s is always drained by warp s
+constexpr int kStageBytes = 24576;   // 3 units of K=2048 (6 rows) or 1 unit of K<=6144
+constexpr int kConsumerWarps = 8;
+constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
+constexpr int kAttnSplits = 9;       // 16 heads x 9 position splits = 144 attention CTAs
+
+struct LayerPtrs {
+    const half* ln1;     // [H]
+    const half* qkv_w;   // [3H, H], RoPE-pair permuted rows
+    const half* qkv_b;   // [3H], original order
+    const half* proj_w;  // [H, H]
+    const half* ln2;     // [H]
+    const half* w12;     // [2*IM, H], w1/w2 interleaved rows
+    const half* cproj;   // [H, IM]
+};
+
+// Per-launch control words, zeroed by the host before every launch.
+struct DecodeControl {
+    unsigned int bar;                  // grid barrier arrivals
+    unsigned int head_ctr[kHeads];     // attention-merge arrivals per head
+    int err;                           // first error code (0 = none)
+    int err_where;                     // diagnostic: phase id of the failure
+    int n_done;                        // steps completed
+    unsigned long long best[2];        // argmax keys, double-buffered by step parity
+};
+
+struct DecodeArgs {
+    const LayerPtrs* layers;  // device array [NL]
+    const half* wte;          // [V, H]
+    const half* lnf;          // [H]
+    const half* lm_head;      // [V, H]
+    half* kc;                 // [NL][max_seqlen][H]
+    half* vc;
+    half* x;                  // [H]   residual stream
+    half* q;                  // [H]   rotated query of the current step
+    half* att;                // [H]   attention output
+    half* act;                // [IM]  SwiGLU output
+    half* logits;             // [V]
+    float* att_part;          // [kHeads * kAttnSplits * 130] split partials (o[128], m, l)
+    DecodeControl* ctl;
+    int* tokens_out;          // [n_steps] device copy of generated tokens (may be null)
+    int* host_tokens;         // mapped host buffer for streaming (may be null)
+    int* host_count;          // mapped host word: number of tokens published
+    const int* forced;        // [n_steps] input tokens when skip_lm (prefill through the decode path)
+    int NL, IM, V, max_seqlen;
+    int first_token, pos0, n_steps;
+    int skip_lm;              // 1: no lm_head; the input of step t+1 is forced[t+1]
+    int stop0, stop1;         // stop ids (-1 = none)
+};
+
+}  // namespace llmdiy

@@ -1,0 +1,116 @@
+// prefill_abi.cu — the prefill-side launchers of the reference ABI:
+// hgemm_swizzle_nn (kernels/hgemm_mma_swizzle.cuh:414-439) and
+// flash_attn_tuned_A with the causal mask (kernels/flash_attn.cu:1854-2179).
+//
+// These are the op-level entry points for callers that hold row-major
+// [K,N] weights and per-head attention buffers, exactly as the reference's
+// prefill does.  They accumulate in fp32 (the reference accumulates the GEMM
+// and the attention scores in fp16).
+#include "ops.cuh"
+
+using namespace llmdiy;
+
+namespace {
+
+inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// C[M,N] = A[M,K] * B[K,N], all row-major fp16, fp32 accumulation.
+// 64x64 output tile per CTA, 256 threads x (4x4) outputs, K staged 16 at a time.
+__global__ void __launch_bounds__(256) gemm_rr_k(const half* __restrict__ A, const half* __restrict__ B,
+                                                  half* __restrict__ C, int M, int N, int K) {
+    __shared__ float As[16][64 + 1];
+    __shared__ float Bs[16][64 + 1];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += 16) {
+        for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+            const int r = i / 16, k = i % 16;
+            const int gm = m0 + r, gk = k0 + k;
+            As[k][r] = (gm < M && gk < K) ? __half2float(A[(size_t)gm * K + gk]) : 0.f;
+            const int kb = i / 64, c = i % 64;
+            const int gkb = k0 + kb, gn = n0 + c;
+            Bs[kb][c] = (gkb < K && gn < N) ? __half2float(B[(size_t)gkb * N + gn]) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[k][ty * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = Bs[k][tx * 4 + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int gm = m0 + ty * 4 + i, gn = n0 + tx * 4 + j;
+            if (gm < M && gn < N) C[(size_t)gm * N + gn] = __float2half_rn(acc[i][j]);
+        }
+}
+
+// Causal single-head attention, one warp per query row (keys 0..row),
+// rows of Q/O at stride_q and of K/V at stride_kv (halves).
+__global__ void __launch_bounds__(256) causal_attn_rows_k(const half* __restrict__ Q, const half* __restrict__ K,
+                                                           const half* __restrict__ V, half* __restrict__ O, int N,
+                                                           int stride_q, int stride_kv) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, dl = (lane & 15) * 8;
+    const int row = blockIdx.x * 8 + warp;
+    if (row >= N) return;
+    float q8[8];
+    unpack8(*reinterpret_cast<const uint4*>(Q + (size_t)row * stride_q + dl), q8);
+    const float scale = 1.0f / sqrtf(128.0f);
+    float m = -INFINITY, l = 0.f, o8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o8[e] = 0.f;
+    attend_rows<false>(K, V, stride_kv, 0, row + 1, q8, scale, m, l, o8);
+    combine_halfwarps(m, l, o8);
+    if (lane < 16) {
+        const float inv = __frcp_rn(l);
+        float of[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) of[e] = o8[e] * inv;
+        *reinterpret_cast<uint4*>(O + (size_t)row * stride_q + dl) = pack8(of);
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int llmdiy_hgemm_swizzle_nn(uint16_t* A, uint16_t* B, uint16_t* C, int M, int N, int K, void* stream) {
+    if (M <= 0 || N <= 0 || K <= 0) return (int)cudaErrorInvalidValue;
+    dim3 grid((N + 63) / 64, (M + 63) / 64);
+    gemm_rr_k<<<grid, 256, 0, S(stream)>>>(reinterpret_cast<const half*>(A), reinterpret_cast<const half*>(B),
+                                           reinterpret_cast<half*>(C), M, N, K);
+    return (int)cudaGetLastError();
+}
+
+// Offsets follow kernels/flash_attn.cu:1904-1909: an override >= 0 is used
+// as given, otherwise the base is QKV_head * N * stride.  O rows use stride_Q.
+int llmdiy_flash_attn_tuned_A(uint16_t* Q, uint16_t* K, uint16_t* V, uint16_t* O, int N, int QKV_head, int stride_Q,
+                              int stride_KV, int K_ofs, int V_ofs, int Q_ofs, int O_ofs, void* stream) {
+    if (N <= 0 || (stride_Q & 7) || (stride_KV & 7)) return (int)cudaErrorInvalidValue;
+    const long long qb = Q_ofs >= 0 ? Q_ofs : (long long)QKV_head * N * stride_Q;
+    const long long kb = K_ofs >= 0 ? K_ofs : (long long)QKV_head * N * stride_KV;
+    const long long vb = V_ofs >= 0 ? V_ofs : (long long)QKV_head * N * stride_KV;
+    const long long ob = O_ofs >= 0 ? O_ofs : (long long)QKV_head * N * stride_Q;
+    const half* q = reinterpret_cast<const half*>(Q) + qb;
+    const half* k = reinterpret_cast<const half*>(K) + kb;
+    const half* v = reinterpret_cast<const half*>(V) + vb;
+    half* o = reinterpret_cast<half*>(O) + ob;
+    // 16-byte vector accesses: every row start must be 16-byte aligned
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    if (!al(q) || !al(k) || !al(v) || !al(o)) return (int)cudaErrorInvalidValue;
+    causal_attn_rows_k<<<(N + 7) / 8, 256, 0, S(stream)>>>(q, k, v, o, N, stride_Q, stride_KV);
+    return (int)cudaGetLastError();
+}
+
+}  // extern "C"

@@ -1,0 +1,315 @@
+"""ctypes binding of libllmdiy_b200.so (include/llmdiy_kernels.h, include/llmdiy_engine.h).
+
+Host-side mirror of the reference's interfaces for Python callers: the
+`Engine` class follows QwenEngine (framework_src/qwen_infer.cu:69-738) --
+construct from a .bin path, reset(), prefill(tokens), step(token, pos) --
+plus generate() for the driver's turn loop (qwen_infer.cu:786-818).  The
+kernel launchers take device addresses (ints, e.g. torch.Tensor.data_ptr())
+and an optional CUDA stream handle, keeping the reference parameter order.
+
+The library is required: importing this module never falls back to another
+implementation, and every call raises LlmdiyError on a non-zero status.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_build", "libllmdiy_b200.so")
+DRIVER_PATH = os.path.join(_HERE, "_build", "qwen_infer_b200")
+INCLUDE_DIR = os.path.join(os.path.dirname(_HERE), "include")
+
+STOP_IDS = (151645, 151643)  # qwen_infer.cu:808
+
+
+class LlmdiyError(RuntimeError):
+    pass
+
+
+class Config(ctypes.Structure):
+    _fields_ = [
+        ("vocab_size", ctypes.c_uint32),
+        ("hidden_size", ctypes.c_uint32),
+        ("num_layers", ctypes.c_uint32),
+        ("num_heads", ctypes.c_uint32),
+        ("intermediate_size", ctypes.c_uint32),
+        ("max_seqlen", ctypes.c_uint32),
+    ]
+
+    def as_dict(self):
+        return {k: int(getattr(self, k)) for k, _ in self._fields_}
+
+
+def make_config(vocab_size=151936, hidden_size=2048, num_layers=24, num_heads=16, intermediate_size=5504,
+                max_seqlen=2048) -> Config:
+    return Config(vocab_size, hidden_size, num_layers, num_heads, intermediate_size, max_seqlen)
+
+
+QWEN_1_8B = dict(vocab_size=151936, hidden_size=2048, num_layers=24, num_heads=16, intermediate_size=5504)
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the sm_100a library (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise LlmdiyError(f"{LIB_PATH} is missing: build it with `make -C llm-inference-diy_b200`")
+    L = ctypes.CDLL(LIB_PATH)
+    P, I, F, U64, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_uint64, ctypes.c_size_t
+    IP = ctypes.POINTER(ctypes.c_int)
+    sig = {
+        "llmdiy_rmsnorm": [P, P, P, I, F, P],
+        "llmdiy_add_bias": [P, P, I, P],
+        "llmdiy_swiglu": [P, P, P, I, P],
+        "llmdiy_fused_qkv_rope_cache": [P, P, P, I, I, I, I, P],
+        "llmdiy_fd_v5_fused": [P, P, P, P, I, I, P],
+        "llmdiy_fd_v5_split_stage1": [P, P, P, P, P, I, I, I, P],
+        "llmdiy_fd_opt_stage2": [P, P, P, I, P],
+        "llmdiy_argmax": [P, P, I, P],
+        "llmdiy_hgemv": [P, P, P, I, I, P],
+        "llmdiy_hgemm_swizzle_nn": [P, P, P, I, I, I, P],
+        "llmdiy_flash_attn_tuned_A": [P, P, P, P, I, I, I, I, I, I, I, I, P],
+        "llmdiy_gather_q_from_qkv": [P, P, I, I, I, P],
+        "llmdiy_gather_kv_from_cache": [P, P, I, I, I, P],
+        "llmdiy_scatter_interleaved": [P, P, I, I, I, P],
+        "llmdiy_transpose_weight": [P, P, I, I, P],
+        "llmdiy_transpose_weight_gpu": [ctypes.POINTER(ctypes.c_void_p), I, I],
+        "llmdiy_qwdf_read_config": [ctypes.c_char_p, ctypes.POINTER(Config)],
+        "llmdiy_qwdf_write_random": [ctypes.c_char_p, ctypes.POINTER(Config), U64, F, I],
+        "llmdiy_qwdf_fill_tensor": [ctypes.POINTER(Config), I, U64, F, SZ, SZ, P, I],
+        "llmdiy_engine_create": [ctypes.c_char_p, I, ctypes.POINTER(P)],
+        "llmdiy_engine_create_random": [ctypes.POINTER(Config), U64, F, I, ctypes.POINTER(P)],
+        "llmdiy_engine_get_config": [P, ctypes.POINTER(Config)],
+        "llmdiy_engine_reset": [P],
+        "llmdiy_engine_prefill": [P, IP, I],
+        "llmdiy_engine_step": [P, I, I, IP],
+        "llmdiy_engine_generate": [P, IP, I, I, I, IP, IP],
+        "llmdiy_engine_decode_async": [P, I, I, I, I, P],
+        "llmdiy_engine_status": [P, IP],
+        "llmdiy_engine_copy_tokens": [P, IP, I],
+        "llmdiy_engine_copy_logits": [P, P],
+        "llmdiy_engine_copy_hidden": [P, P],
+        "llmdiy_engine_copy_kv": [P, I, I, I, P, P],
+        "llmdiy_engine_num_sms": [P],
+    }
+    for name, args in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_int
+    L.llmdiy_engine_destroy.argtypes = [P]
+    L.llmdiy_engine_destroy.restype = None
+    L.llmdiy_engine_last_error.argtypes = [P]
+    L.llmdiy_engine_last_error.restype = ctypes.c_char_p
+    _lib = L
+    return L
+
+
+def declared_symbols() -> list[str]:
+    """Every function declared in include/*.h (for the export check)."""
+    names = []
+    for fn in sorted(os.listdir(INCLUDE_DIR)):
+        if fn.endswith(".h"):
+            text = open(os.path.join(INCLUDE_DIR, fn)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            names += re.findall(r"\b(llmdiy_\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+def _check(rc: int, what: str, engine=None):
+    if rc != 0:
+        msg = ""
+        if engine is not None:
+            m = lib().llmdiy_engine_last_error(engine)
+            msg = m.decode() if m else ""
+        raise LlmdiyError(f"{what} failed with status {rc} {msg}".strip())
+
+
+# ----------------------------------------------------------------- kernels
+def _p(x):
+    return None if x is None else ctypes.c_void_p(int(x))
+
+
+def rmsnorm(out, inp, weight, d, eps=1e-6, stream=None):
+    _check(lib().llmdiy_rmsnorm(_p(out), _p(inp), _p(weight), d, eps, _p(stream)), "rmsnorm")
+
+
+def add_bias(out, bias, size, stream=None):
+    _check(lib().llmdiy_add_bias(_p(out), _p(bias), size, _p(stream)), "add_bias")
+
+
+def swiglu(out, w1o, w2o, size, stream=None):
+    _check(lib().llmdiy_swiglu(_p(out), _p(w1o), _p(w2o), size, _p(stream)), "swiglu")
+
+
+def fused_qkv_rope_cache(qkv, kc, vc, pos, max_seqlen, num_heads, head_dim, stream=None):
+    _check(lib().llmdiy_fused_qkv_rope_cache(_p(qkv), _p(kc), _p(vc), pos, max_seqlen, num_heads, head_dim,
+                                             _p(stream)), "fused_qkv_rope_cache")
+
+
+def fd_v5_fused(Q, K, V, O, L, stride, stream=None):
+    _check(lib().llmdiy_fd_v5_fused(_p(Q), _p(K), _p(V), _p(O), L, stride, _p(stream)), "fd_v5_fused")
+
+
+def fd_v5_split_stage1(Q, K, V, Opart, LSE, L, num_chunks, stride, stream=None):
+    _check(lib().llmdiy_fd_v5_split_stage1(_p(Q), _p(K), _p(V), _p(Opart), _p(LSE), L, num_chunks, stride,
+                                           _p(stream)), "fd_v5_split_stage1")
+
+
+def fd_opt_stage2(Opart, LSE, O, num_chunks, stream=None):
+    _check(lib().llmdiy_fd_opt_stage2(_p(Opart), _p(LSE), _p(O), num_chunks, _p(stream)), "fd_opt_stage2")
+
+
+def argmax(out, logits, V, stream=None):
+    _check(lib().llmdiy_argmax(_p(out), _p(logits), V, _p(stream)), "argmax")
+
+
+def hgemv(A, B, C, N, K, stream=None):
+    _check(lib().llmdiy_hgemv(_p(A), _p(B), _p(C), N, K, _p(stream)), "hgemv")
+
+
+def hgemm_swizzle_nn(A, B, C, M, N, K, stream=None):
+    _check(lib().llmdiy_hgemm_swizzle_nn(_p(A), _p(B), _p(C), M, N, K, _p(stream)), "hgemm_swizzle_nn")
+
+
+def flash_attn_tuned_A(Q, K, V, O, N, QKV_head, stride_Q, stride_KV, K_ofs=-1, V_ofs=-1, Q_ofs=-1, O_ofs=-1,
+                       stream=None):
+    _check(lib().llmdiy_flash_attn_tuned_A(_p(Q), _p(K), _p(V), _p(O), N, QKV_head, stride_Q, stride_KV, K_ofs,
+                                           V_ofs, Q_ofs, O_ofs, _p(stream)), "flash_attn_tuned_A")
+
+
+def gather_q_from_qkv(qkv, buf, N, num_heads, head_dim=128, stream=None):
+    _check(lib().llmdiy_gather_q_from_qkv(_p(qkv), _p(buf), N, num_heads, head_dim, _p(stream)), "gather_q")
+
+
+def gather_kv_from_cache(cache, buf, N, num_heads, head_dim=128, stream=None):
+    _check(lib().llmdiy_gather_kv_from_cache(_p(cache), _p(buf), N, num_heads, head_dim, _p(stream)), "gather_kv")
+
+
+def scatter_interleaved(src, dst, N, num_heads, dst_cols, stream=None):
+    _check(lib().llmdiy_scatter_interleaved(_p(src), _p(dst), N, num_heads, dst_cols, _p(stream)), "scatter")
+
+
+def transpose_weight(out, inp, rows, cols, stream=None):
+    _check(lib().llmdiy_transpose_weight(_p(out), _p(inp), rows, cols, _p(stream)), "transpose_weight")
+
+
+# ----------------------------------------------------------------- QWDF files
+def write_random_bin(path: str, cfg: Config, seed: int, std_dev: float = 0.02, nthreads: int = 8):
+    _check(lib().llmdiy_qwdf_write_random(path.encode(), ctypes.byref(cfg), seed, std_dev, nthreads),
+           "qwdf_write_random")
+
+
+def read_bin_config(path: str) -> Config:
+    c = Config()
+    _check(lib().llmdiy_qwdf_read_config(path.encode(), ctypes.byref(c)), "qwdf_read_config")
+    return c
+
+
+def fill_tensor(cfg: Config, tensor_id: int, seed: int, first: int, n: int, std_dev: float = 0.02, nthreads=8):
+    import numpy as np
+    out = np.empty(n, dtype=np.uint16)
+    _check(lib().llmdiy_qwdf_fill_tensor(ctypes.byref(cfg), tensor_id, seed, std_dev, first, n,
+                                         out.ctypes.data_as(ctypes.c_void_p), nthreads), "qwdf_fill_tensor")
+    return out
+
+
+# ----------------------------------------------------------------- engine
+def _ints(seq):
+    arr = (ctypes.c_int * max(1, len(seq)))(*seq)
+    return arr
+
+
+class Engine:
+    """QwenEngine on one B200 (framework_src/qwen_infer.cu:69-738)."""
+
+    def __init__(self, bin_path: str | None = None, device: int = 0, *, config: Config | None = None,
+                 seed: int = 0, std_dev: float = 0.02):
+        self._h = ctypes.c_void_p()
+        L = lib()
+        if bin_path is not None:
+            rc = L.llmdiy_engine_create(bin_path.encode(), device, ctypes.byref(self._h))
+        else:
+            if config is None:
+                raise ValueError("either bin_path or config is required")
+            rc = L.llmdiy_engine_create_random(ctypes.byref(config), seed, std_dev, device, ctypes.byref(self._h))
+        if rc != 0:
+            raise LlmdiyError(f"engine create failed with status {rc}")
+        c = Config()
+        L.llmdiy_engine_get_config(self._h, ctypes.byref(c))
+        self.config = c
+
+    def close(self):
+        if self._h:
+            lib().llmdiy_engine_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _chk(self, rc, what):
+        _check(rc, what, self._h)
+
+    def reset(self):
+        self._chk(lib().llmdiy_engine_reset(self._h), "reset")
+
+    def prefill(self, tokens):
+        self._chk(lib().llmdiy_engine_prefill(self._h, _ints(tokens), len(tokens)), "prefill")
+
+    def step(self, token: int, pos: int) -> int:
+        nxt = ctypes.c_int()
+        self._chk(lib().llmdiy_engine_step(self._h, token, pos, ctypes.byref(nxt)), "step")
+        return nxt.value
+
+    def generate(self, prompt, max_new: int, stop_on_eos: bool = True) -> list[int]:
+        out = (ctypes.c_int * max(1, max_new))()
+        n = ctypes.c_int()
+        self._chk(lib().llmdiy_engine_generate(self._h, _ints(prompt), len(prompt), max_new, int(stop_on_eos), out,
+                                               ctypes.byref(n)), "generate")
+        return list(out[: n.value])
+
+    def decode_async(self, first_token: int, pos: int, n_steps: int, stop_on_eos=False, stream=None):
+        self._chk(lib().llmdiy_engine_decode_async(self._h, first_token, pos, n_steps, int(stop_on_eos), _p(stream)),
+                  "decode_async")
+
+    def status(self) -> int:
+        n = ctypes.c_int()
+        self._chk(lib().llmdiy_engine_status(self._h, ctypes.byref(n)), "status")
+        return n.value
+
+    def tokens(self, n: int) -> list[int]:
+        out = (ctypes.c_int * max(1, n))()
+        self._chk(lib().llmdiy_engine_copy_tokens(self._h, out, n), "copy_tokens")
+        return list(out[:n])
+
+    def logits(self):
+        import numpy as np
+        out = np.empty(self.config.vocab_size, dtype=np.uint16)
+        self._chk(lib().llmdiy_engine_copy_logits(self._h, out.ctypes.data_as(ctypes.c_void_p)), "copy_logits")
+        return out.view(np.float16)
+
+    def hidden(self):
+        import numpy as np
+        out = np.empty(self.config.hidden_size, dtype=np.uint16)
+        self._chk(lib().llmdiy_engine_copy_hidden(self._h, out.ctypes.data_as(ctypes.c_void_p)), "copy_hidden")
+        return out.view(np.float16)
+
+    def kv(self, layer: int, pos0: int, n: int):
+        import numpy as np
+        H = self.config.hidden_size
+        k = np.empty((n, H), dtype=np.uint16)
+        v = np.empty((n, H), dtype=np.uint16)
+        self._chk(lib().llmdiy_engine_copy_kv(self._h, layer, pos0, n, k.ctypes.data_as(ctypes.c_void_p),
+                                              v.ctypes.data_as(ctypes.c_void_p)), "copy_kv")
+        return k.view(np.float16), v.view(np.float16)
+
+    @property
+    def num_sms(self) -> int:
+        return lib().llmdiy_engine_num_sms(self._h)

@@ -1,0 +1,212 @@
+"""Op-level parity of the sm_100a kernels (through the C ABI) with the CPU
+oracle and, where oracle/_ref is built, with the reference's own kernels
+JIT-run from compute_89 PTX on the same GPU and the same inputs.
+
+Tolerances (north_star / kernels/unit_tests/run_tests.cu): ArgMax and pure
+data movement bit-exact; attention outputs within 1e-3 abs; RMSNorm, bias,
+RoPE within one fp16 ulp of the oracle and bit-exact against the reference
+kernels; GEMV 1e-3; GEMM (values x0.1) 2e-2."""
+import numpy as np
+import pytest
+
+import llmdiy_b200 as L
+import refmath
+from gpu_util import dev, f16_ulp, host, max_abs, ref_kernels, torch, zeros16
+
+pytestmark = pytest.mark.gpu
+
+H = 2048
+
+
+@pytest.fixture(scope="module")
+def ref():
+    return ref_kernels()
+
+
+def test_rmsnorm_bit_exact(oracle, rng, ref):
+    x = refmath.h(rng.standard_normal(H))
+    w = refmath.h(rng.random(H) + 0.5)
+    dx, dw, out = dev(x), dev(w), zeros16(H)
+    L.rmsnorm(out.data_ptr(), dx.data_ptr(), dw.data_ptr(), H, 1e-6)
+    got = host(out)
+    exp = oracle.rmsnorm(x, w)
+    assert np.all(np.abs(got.astype(np.float32) - exp.astype(np.float32)) <= f16_ulp(exp))
+    if ref is not None:
+        r = zeros16(H)
+        ref.rmsnorm(r.data_ptr(), dx.data_ptr(), dw.data_ptr(), H, 1e-6)
+        assert np.array_equal(got.view(np.uint16), host(r).view(np.uint16))
+
+
+@pytest.mark.parametrize("n", [2048, 6144, 5504, 37])
+def test_add_bias_exact(oracle, rng, ref, n):
+    o = refmath.h(rng.random(n) - 0.5)
+    b = refmath.h(rng.random(n) - 0.5)
+    do, db = dev(o), dev(b)
+    L.add_bias(do.data_ptr(), db.data_ptr(), n)
+    assert np.array_equal(host(do).view(np.uint16), oracle.add_bias(o, b).view(np.uint16))
+
+
+def test_swiglu(oracle, rng, ref):
+    n = 5504
+    a = refmath.h(rng.standard_normal(n))
+    b = refmath.h(rng.standard_normal(n))
+    da, db, out = dev(a), dev(b), zeros16(n)
+    L.swiglu(out.data_ptr(), da.data_ptr(), db.data_ptr(), n)
+    got = host(out)
+    assert max_abs(got, oracle.swiglu(a, b)) < 1e-3 * 4  # values up to ~4: one fp16 ulp
+    assert np.all(np.abs(got.astype(np.float32) - oracle.swiglu(a, b).astype(np.float32))
+                  <= f16_ulp(oracle.swiglu(a, b)) * 1.01)
+    if ref is not None:
+        r = zeros16(n)
+        ref.swiglu(r.data_ptr(), da.data_ptr(), db.data_ptr(), n)
+        assert np.array_equal(got.view(np.uint16), host(r).view(np.uint16))
+
+
+@pytest.mark.parametrize("pos", [0, 3, 127, 383, 4095])
+def test_rope_cache(oracle, rng, ref, pos):
+    S = 4096
+    qkv = refmath.h(rng.standard_normal(3 * H))
+    dq = dev(qkv)
+    kc, vc = zeros16(S * H), zeros16(S * H)
+    L.fused_qkv_rope_cache(dq.data_ptr(), kc.data_ptr(), vc.data_ptr(), pos, S, 16, 128)
+    gq, gk, gv = host(dq), host(kc), host(vc)
+    oq, ok, ov = oracle.fused_qkv_rope_cache(qkv, np.zeros(S * H, np.float16), np.zeros(S * H, np.float16), pos, S)
+    assert max_abs(gq, oq) <= 2e-3 and max_abs(gk, ok) <= 2e-3  # fast-math sincos vs libm, |q|<~4
+    assert np.array_equal(gv.view(np.uint16), ov.view(np.uint16))
+    if ref is not None:
+        dq2, kc2, vc2 = dev(qkv), zeros16(S * H), zeros16(S * H)
+        ref.fused_qkv_rope_cache(dq2.data_ptr(), kc2.data_ptr(), vc2.data_ptr(), pos, S, 16, 128)
+        assert np.array_equal(gq.view(np.uint16), host(dq2).view(np.uint16))
+        assert np.array_equal(gk.view(np.uint16), host(kc2).view(np.uint16))
+
+
+@pytest.mark.parametrize("case", ["unique", "all_equal", "lanes", "warps", "nan_inf", "neg_zero", "random_ties",
+                                  "all_neg_inf", "small_vocab"])
+def test_argmax_bit_exact(oracle, rng, ref, case):
+    V = 151936 if case != "small_vocab" else 1000
+    ipt = (V + 511) // 512
+    lg = refmath.h(rng.standard_normal(V))
+    if case == "unique":
+        lg[777] = 60.0
+    elif case == "all_equal":
+        lg[:] = 1.5
+    elif case == "lanes":
+        lg[8 * ipt + 3] = lg[16 * ipt + 1] = lg[24 * ipt] = 9.0
+    elif case == "warps":
+        lg[(3 * 32) * ipt] = lg[(8 * 32) * ipt] = lg[(12 * 32 + 5) * ipt] = 9.0
+    elif case == "nan_inf":
+        lg[10] = np.nan
+        lg[5000] = np.inf
+        lg[90000] = np.inf
+    elif case == "neg_zero":
+        lg[:] = -2.0
+        lg[40 * ipt] = -0.0
+        lg[64 * ipt] = 0.0
+    elif case == "random_ties":
+        lg = refmath.h(np.round(rng.standard_normal(V) * 2) / 2)
+    elif case == "all_neg_inf":
+        lg[:] = -np.inf
+    d = dev(lg)
+    out = torch().zeros(1, dtype=torch().int32, device="cuda")
+    L.argmax(out.data_ptr(), d.data_ptr(), V)
+    got = int(host(out)[0])
+    assert got == oracle.argmax(lg) == refmath.argmax_reference(lg)
+    if ref is not None:
+        r = torch().zeros(1, dtype=torch().int32, device="cuda")
+        ref.argmax(r.data_ptr(), d.data_ptr(), V)
+        assert got == int(host(r)[0])
+
+
+@pytest.mark.parametrize("N,K", [(6144, 2048), (2048, 5504), (151936, 2048), (100, 64), (37, 128)])
+def test_hgemv_kn(oracle, rng, N, K):
+    A = refmath.h(rng.standard_normal(K))
+    B = refmath.h(rng.standard_normal((K, N)) * 0.02)
+    dA, dB, C = dev(A), dev(B), zeros16(N)
+    L.hgemv(dA.data_ptr(), dB.data_ptr(), C.data_ptr(), N, K)
+    assert max_abs(host(C), oracle.hgemv_kn(A, B)) < 1e-2 * max(1.0, np.sqrt(K / 2048))
+
+
+@pytest.mark.parametrize("L_,stride", [(1, 2048), (37, 2048), (256, 2048), (256, 128), (300, 2048)])
+def test_fd_v5_fused(oracle, rng, ref, L_, stride):
+    q = refmath.h(rng.standard_normal(128))
+    K = refmath.h(rng.standard_normal(L_ * stride))
+    V = refmath.h(rng.standard_normal(L_ * stride))
+    dq, dK, dV, O = dev(q), dev(K), dev(V), zeros16(128)
+    L.fd_v5_fused(dq.data_ptr(), dK.data_ptr(), dV.data_ptr(), O.data_ptr(), L_, stride)
+    got = host(O)
+    Le = min(L_, 256)  # the reference fused kernel covers at most 256 rows
+    assert max_abs(got, oracle.attention_q1(q, K, V, Le, stride)) < 1e-3
+    if ref is not None:
+        r = zeros16(128)
+        ref.fd_v5_fused(dq.data_ptr(), dK.data_ptr(), dV.data_ptr(), r.data_ptr(), L_, stride)
+        assert max_abs(got, host(r)) < 1e-3
+
+
+@pytest.mark.parametrize("L_,stride", [(257, 2048), (1024, 128), (1024, 2048), (4097, 2048)])
+def test_fd_v5_split(oracle, rng, ref, L_, stride):
+    nc = (L_ + 255) // 256
+    q = refmath.h(rng.standard_normal(128))
+    K = refmath.h(rng.standard_normal(L_ * stride))
+    V = refmath.h(rng.standard_normal(L_ * stride))
+    dq, dK, dV = dev(q), dev(K), dev(V)
+    Op, lse, O = zeros16(nc * 128), torch().zeros(nc, dtype=torch().float32, device="cuda"), zeros16(128)
+    L.fd_v5_split_stage1(dq.data_ptr(), dK.data_ptr(), dV.data_ptr(), Op.data_ptr(), lse.data_ptr(), L_, nc, stride)
+    L.fd_opt_stage2(Op.data_ptr(), lse.data_ptr(), O.data_ptr(), nc)
+    oOp, olse = oracle.fd_split_stage1(q, K, V, L_, nc, stride)
+    assert max_abs(host(Op), oOp) < 1e-3
+    assert max_abs(host(lse), olse) < 1e-4 * max(1.0, float(np.max(np.abs(olse))))
+    assert max_abs(host(O), refmath.attention(q, K, V, L_, stride)) < 1e-3
+    if ref is not None:
+        rOp, rl, rO = zeros16(nc * 128), torch().zeros(nc, dtype=torch().float32, device="cuda"), zeros16(128)
+        ref.fd_v5_split_stage1(dq.data_ptr(), dK.data_ptr(), dV.data_ptr(), rOp.data_ptr(), rl.data_ptr(), L_, nc,
+                               stride)
+        ref.fd_opt_stage2(rOp.data_ptr(), rl.data_ptr(), rO.data_ptr(), nc)
+        assert max_abs(host(O), host(rO)) < 1e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (127, 6144, 2048), (300, 200, 100)])
+def test_hgemm_swizzle_nn(oracle, rng, M, N, K):
+    A = refmath.h((rng.random((M, K)) - 0.5) * 0.1)
+    B = refmath.h((rng.random((K, N)) - 0.5) * 0.1)
+    dA, dB, C = dev(A), dev(B), zeros16(M * N)
+    L.hgemm_swizzle_nn(dA.data_ptr(), dB.data_ptr(), C.data_ptr(), M, N, K)
+    assert max_abs(host(C).reshape(M, N), oracle.hgemm_kn(A, B)) < 2e-2
+
+
+@pytest.mark.parametrize("N", [1, 100, 257])
+def test_flash_attn_causal(oracle, rng, ref, N):
+    Q = refmath.h(rng.standard_normal(N * 128))
+    K = refmath.h(rng.standard_normal(N * 128))
+    V = refmath.h(rng.standard_normal(N * 128))
+    dQ, dK, dV, O = dev(Q), dev(K), dev(V), zeros16(N * 128)
+    L.flash_attn_tuned_A(dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), O.data_ptr(), N, 1, 128, 128, 0, 0, 0, 0)
+    got = host(O)
+    assert max_abs(got, oracle.causal_attention(Q, K, V, N, 128, 128)) < 1e-3
+    if ref is not None:
+        r = zeros16(N * 128)
+        ref.flash_attn_causal_head(dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), r.data_ptr(), N)
+        # the reference accumulates S and P.V in fp16 (flash_attn.cu:2002-2005)
+        assert max_abs(got, host(r)) < 3e-2
+
+
+def test_gather_scatter_transpose_exact(rng, ref):
+    N, nh = 77, 16
+    qkv = refmath.h(rng.standard_normal(N * 3 * H))
+    dq, buf = dev(qkv), zeros16(nh * N * 128)
+    L.gather_q_from_qkv(dq.data_ptr(), buf.data_ptr(), N, nh)
+    g = host(buf).reshape(nh, N, 128)
+    exp = qkv.reshape(N, 3 * H)[:, :H].reshape(N, nh, 128).transpose(1, 0, 2)
+    assert np.array_equal(g.view(np.uint16), np.ascontiguousarray(exp).view(np.uint16))
+    cache = refmath.h(rng.standard_normal(N * H))
+    dc, buf2 = dev(cache), zeros16(nh * N * 128)
+    L.gather_kv_from_cache(dc.data_ptr(), buf2.data_ptr(), N, nh)
+    g2 = host(buf2).reshape(nh, N, 128)
+    assert np.array_equal(g2.view(np.uint16), np.ascontiguousarray(cache.reshape(N, nh, 128).transpose(1, 0, 2))
+                          .view(np.uint16))
+    back = zeros16(N * H)
+    L.scatter_interleaved(buf2.data_ptr(), back.data_ptr(), N, nh, H)
+    assert np.array_equal(host(back).view(np.uint16), cache.view(np.uint16))
+    W = refmath.h(rng.standard_normal((300, 130)))
+    dW, out = dev(W), zeros16(300 * 130)
+    L.transpose_weight(out.data_ptr(), dW.data_ptr(), 300, 130)
+    assert np.array_equal(host(out).reshape(130, 300).view(np.uint16), np.ascontiguousarray(W.T).view(np.uint16))
