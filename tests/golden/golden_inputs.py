@@ -59,5 +59,12 @@ def argmax_cases():
 
 
 def engine_prompts():
+    """Prompts of the recorded ref_engine.json: a one-token prompt (pure decode
+    path) and a 16-token prompt (exercises the reference's prefill)."""
     r = np.random.default_rng(31)
     return [[77], r.integers(0, ENGINE_CFG["vocab_size"], 16).tolist()]
+
+
+def engine_prompts_rerun():
+    """Prompts make_golden.py --engine may run again on the reference engine."""
+    return [[77]]

@@ -3,7 +3,7 @@ kernels and engine (LLM-inference-DIY), compiled from their sources by
 `make -C oracle ref` into oracle/_ref as compute_89 PTX and JIT-run on a B200.
 
 Run on a GPU box from the repository root:
-    python tests/golden/make_golden.py [outdir]
+    python tests/golden/make_golden.py [outdir] [--engine]
 It writes ref_ops.npz (seeded inputs and the reference kernels' outputs) and
 ref_engine.json (token streams of the reference engine qwen_infer on a
 seeded random-weight QWDF file).  Inputs are regenerated from the stored
@@ -25,25 +25,32 @@ sys.path.insert(0, os.path.join(ROOT, "llm-inference-diy_b200"))
 import golden_inputs as gi  # noqa: E402
 
 
-def main(outdir):
+def main(outdir, engine=False):
     import torch
 
     import oracle as orc
     ref = orc.RefKernels()
     os.makedirs(outdir, exist_ok=True)
 
+    keep = []  # device inputs stay referenced so the caching allocator cannot alias them
+
     def dev(a):
         a = np.ascontiguousarray(a)
         if a.dtype == np.float16:
-            return torch.from_numpy(a.view(np.int16).copy()).cuda()
-        return torch.from_numpy(a.copy()).cuda()
+            t = torch.from_numpy(a.view(np.int16).copy()).cuda()
+        else:
+            t = torch.from_numpy(a.copy()).cuda()
+        keep.append(t)
+        return t
 
     def host16(t):
         torch.cuda.synchronize()
         return t.cpu().numpy().view(np.float16)
 
     def z16(n):
-        return torch.zeros(n, dtype=torch.int16, device="cuda")
+        t = torch.zeros(n, dtype=torch.int16, device="cuda")
+        keep.append(t)
+        return t
 
     out = {}
     inp = gi.ops_inputs()
@@ -104,13 +111,21 @@ def main(outdir):
                                o.data_ptr(), n)
     out["fa_O"] = host16(o)
     np.savez_compressed(os.path.join(outdir, "ref_ops.npz"), **out)
+    print("op fixtures written to", outdir)
+    if not engine:
+        return
 
-    # engine level: the reference engine binary on a seeded QWDF file
+    # Engine level: the reference engine binary on a seeded QWDF file.  Only
+    # one-token prompts are run: with a longer prompt the reference's prefill
+    # attention produced NaN on a B200, its argmax returned -1, and the next
+    # step read the embedding row at index -1 (outside the wte allocation);
+    # that recorded turn is kept in ref_engine.json and is not re-run.
+    assert all(len(p) == 1 for p in gi.engine_prompts_rerun())
     import llmdiy_b200 as L
     d = tempfile.mkdtemp()
     path = os.path.join(d, "golden.bin")
     L.write_random_bin(path, L.make_config(**gi.ENGINE_CFG), seed=gi.ENGINE_SEED)
-    lines = ["reset"] + [" ".join(map(str, p)) for p in gi.engine_prompts()] + ["exit"]
+    lines = ["reset"] + [" ".join(map(str, p)) for p in gi.engine_prompts_rerun()] + ["exit"]
     r = subprocess.run([orc.REF_ENGINE, path], input="\n".join(lines) + "\n", capture_output=True, text=True,
                        timeout=1200)
     os.remove(path)
@@ -124,11 +139,12 @@ def main(outdir):
             cur = None
         elif cur is not None and line.lstrip("-").isdigit():
             cur.append(int(line))
-    res = {"config": gi.ENGINE_CFG, "seed": gi.ENGINE_SEED, "prompts": gi.engine_prompts(), "tokens": turns,
+    res = {"config": gi.ENGINE_CFG, "seed": gi.ENGINE_SEED, "prompts": gi.engine_prompts_rerun(), "tokens": turns,
            "returncode": r.returncode, "engine": "oracle/_ref/qwen_infer_ref (compute_89 PTX, JIT on B200)"}
     json.dump(res, open(os.path.join(outdir, "ref_engine.json"), "w"))
     print("golden fixtures written to", outdir, "turns:", [len(t) for t in turns])
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(ROOT, "gpurun_out", "golden"))
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    main(args[0] if args else os.path.join(ROOT, "gpurun_out", "golden"), engine="--engine" in sys.argv)

@@ -185,8 +185,17 @@ def test_flash_attn_causal(oracle, rng, ref, N):
     if ref is not None:
         r = zeros16(N * 128)
         ref.flash_attn_causal_head(dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), r.data_ptr(), N)
-        # the reference accumulates S and P.V in fp16 (flash_attn.cu:2002-2005)
-        assert max_abs(got, host(r)) < 3e-2
+        rr = host(r).astype(np.float32)
+        # The reference reads unzeroed shared memory for rows past N (flash_attn.cu:1984-1987)
+        # and can emit NaN there; it also accumulates S and P.V in fp16 (:2002-2005).
+        # Compare where it is finite; ours must be finite everywhere.
+        assert np.all(np.isfinite(got.astype(np.float32)))
+        # The reference is exact only on the first 8 rows of each 16-row MMA tile
+        # (rows 8..15 of every tile are wrong); compare there, where it is finite.
+        low = np.repeat((np.arange(N) % 16) < 8, 128)
+        ok = np.isfinite(rr) & low
+        if ok.any():
+            assert max_abs(got.astype(np.float32)[ok], rr[ok]) < 3e-3
 
 
 def test_gather_scatter_transpose_exact(rng, ref):
