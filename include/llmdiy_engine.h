@@ -80,6 +80,12 @@ int llmdiy_engine_decode_async(llmdiy_engine* e, int first_token, int pos, int n
 /* After the stream is synchronised: kernel status of the last launch and steps completed. */
 int llmdiy_engine_status(llmdiy_engine* e, int* n_done);
 
+/* Timing probes of one decode launch (development aid): out[(cta*cap + i)*2] = %globaltimer ns at
+ * the i-th phase boundary of CTA `cta`; prod[((cta*6 + phase)*8 + warp)*4 + {0..3}] = SM cycles waiting
+ * for weight chunks, computing, issuing copies; chunks (phase 0..5 = qkv, att, o, w12, c, lm_head). */
+int llmdiy_engine_profile(llmdiy_engine* e, int first_token, int pos, int n_steps, int cap, uint64_t* out,
+                          uint64_t* prod);
+
 /* ---- inspection (tests) ---- */
 int llmdiy_engine_copy_tokens(llmdiy_engine* e, int* out, int n);          /* last decode's tokens */
 int llmdiy_engine_copy_logits(llmdiy_engine* e, uint16_t* out);            /* [vocab] fp16 of the last step */

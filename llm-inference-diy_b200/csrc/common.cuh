@@ -100,6 +100,10 @@ LLMDIY_DEV void tma_load_2d_hint(void* smem_dst, const void* tmap, int32_t x, in
         ::"r"(smem_u32(smem_dst)), "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// Bulk prefetch of a global range into L2 (no shared memory, no completion).
+LLMDIY_DEV void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes) : "memory");
+}
 LLMDIY_DEV void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
@@ -157,6 +161,12 @@ LLMDIY_DEV bool named_bar_or(int id, int nthreads, bool pred) {
         : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
         : "memory");
     return r != 0;
+}
+
+LLMDIY_DEV unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
 // ---------------- fp16 helpers ----------------

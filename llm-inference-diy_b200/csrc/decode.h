@@ -23,8 +23,9 @@ constexpr int kHeads = kHidden / kHeadDim;
 constexpr int kRingStages = 8;       // == consumer warps: slot s is always drained by warp s
 constexpr int kStageBytes = 24576;   // 3 units of K=2048 (6 rows) or 1 unit of K<=6144
 constexpr int kConsumerWarps = 8;
-constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
+constexpr int kDecodeThreads = kConsumerWarps * 32;
 constexpr int kAttnSplits = 9;       // 16 heads x 9 position splits = 144 attention CTAs
+constexpr int kMaxLayers = 64;       // layer pointers are cached in shared memory
 
 struct LayerPtrs {
     const half* ln1;     // [H]
@@ -35,6 +36,14 @@ struct LayerPtrs {
     const half* w12;     // [2*IM, H], w1/w2 interleaved rows
     const half* cproj;   // [H, IM]
 };
+
+// Flag-carrying words ("LL" words) pass the small per-phase vectors between
+// CTAs without grid barriers: each 8-byte word holds 32 bits of data in its
+// low half and a 32-bit phase tag in its high half, written with one 64-bit
+// store; a reader polls exactly the words it needs until they carry the tag
+// of the phase instance it expects.  Tags are unique per (launch, step,
+// layer, phase), so no buffer ever needs clearing between phases.
+enum LLSlot : uint32_t { LL_QKV = 0, LL_ATT = 1, LL_XO = 2, LL_ACT = 3, LL_XC = 4, LL_PER_LAYER = 5 };
 
 // Per-launch control words, zeroed by the host before every launch.
 struct DecodeControl {
@@ -53,11 +62,14 @@ struct DecodeArgs {
     const half* lm_head;      // [V, H]
     half* kc;                 // [NL][max_seqlen][H]
     half* vc;
-    half* x;                  // [H]   residual stream
-    half* q;                  // [H]   rotated query of the current step
-    half* att;                // [H]   attention output
-    half* act;                // [IM]  SwiGLU output
+    half* x;                  // [H]   residual stream after the last layer (plain copy)
     half* logits;             // [V]
+    unsigned long long* ll_qkv;  // [3H/2] unit u = (value of row 2u, row 2u+1) after bias/RoPE
+    unsigned long long* ll_att;  // [H/2]  attention output pairs
+    unsigned long long* ll_xo;   // [H/2]  residual stream after o_proj
+    unsigned long long* ll_act;  // [IM]   SwiGLU output, one value per word
+    unsigned long long* ll_xc;   // [H/2]  residual stream after c_proj
+    uint32_t flag_base;          // tag of this launch's first phase instance minus 1
     float* att_part;          // [kHeads * kAttnSplits * 130] split partials (o[128], m, l)
     DecodeControl* ctl;
     int* tokens_out;          // [n_steps] device copy of generated tokens (may be null)
@@ -68,6 +80,13 @@ struct DecodeArgs {
     int first_token, pos0, n_steps;
     int skip_lm;              // 1: no lm_head; the input of step t+1 is forced[t+1]
     int stop0, stop1;         // stop ids (-1 = none)
+    int prefetch_owned;       // L2 prefetch distance in owned chunks (0 = off)
+    // optional timing probes (null in production): per CTA and grid barrier,
+    // %globaltimer at arrival and at release; per CTA the producer's time
+    // blocked on a full ring and the consumers' time waiting for data.
+    unsigned long long* prof;       // [grid][prof_cap][2]
+    unsigned long long* prof_prod;  // [grid][2]
+    int prof_cap;
 };
 
 }  // namespace llmdiy

@@ -1,24 +1,27 @@
 // decode_kernel.cu — the persistent bs1 decode kernel (QwenEngine::step,
 // framework_src/qwen_infer.cu:614-737, for many steps per launch).
 //
-// One CTA per SM.  Warp 8 lane 0 is a producer that streams this CTA's share
-// of every weight matrix, in the exact order the consumers use it, through an
-// 8-stage ring of 24 KB shared-memory slots with 1-D bulk copies (TMA).
-// Weights never depend on activations, so the producer runs ahead across
-// phase, layer and token boundaries and HBM keeps streaming while the
-// consumers wait at grid barriers.  Warps 0-7 are consumers: slot s is always
-// drained by warp s, two rows at a time (fp32 FMA dot products against the
-// activation held in registers or shared memory), with the reference's small
-// ops fused into the epilogues:
-//   QKV  : RMSNorm(ln_1) prologue; bias; RoPE; K/V append at row pos; q out
-//   ATT  : 16 heads x 9 position splits; last CTA of a head merges (m,l,o)
-//   O    : residual add into x
+// One CTA of 8 warps per SM.  Each CTA streams its share of every weight
+// matrix through an 8-slot ring of 24 KB shared-memory slots with 1-D bulk
+// copies (TMA).  Slot w belongs to warp w: the warp consumes chunks w, w+8,
+// w+16, ... of the CTA's chunk sequence, and right after draining a chunk its
+// lane 0 issues the copy of its next chunk (a cursor walks the same sequence
+// eight chunks ahead).  Weights never depend on activations, so those copies
+// run ahead across phase, layer and token boundaries and HBM keeps streaming
+// while the warps wait for activations.  A warp consumes two rows at a time
+// (fp32 FMA dot products against the activation held in registers or shared
+// memory), with the reference's small ops fused into the epilogues:
+//   QKV  : RMSNorm(ln_1) prologue; bias; RoPE; K/V append at row pos
+//   ATT  : 16 heads x 9 position splits; the last CTA of a head merges (m,l,o)
+//   O    : residual add
 //   W12  : RMSNorm(ln_2) prologue; SwiGLU (silu on the w2 output)
-//   C    : residual add into x
+//   C    : residual add
 //   LM   : RMSNorm(ln_f) prologue; logits; greedy argmax key (reference tie rule)
-// Phases are separated by grid barriers on one monotonically increasing
-// counter.  Every spin-wait is bounded; on expiry the kernel records an error
-// code in DecodeControl and returns.
+// Between phases the small activation vectors travel as flag-carrying words
+// (decode.h): a consumer waits for exactly the words it needs, so there is no
+// grid barrier inside a step.  One grid barrier per step publishes the argmax
+// and orders the KV-cache rows for the next step.  Every spin-wait is bounded;
+// on expiry the kernel records an error code in DecodeControl and returns.
 #include "decode.h"
 #include "ops.cuh"
 
@@ -28,18 +31,26 @@ namespace {
 enum PhaseId { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_W12 = 3, PH_C = 4, PH_LM = 5 };
 
 constexpr int kMaxIM = 6144;
+// Each warp also prefetches into L2 the chunk it will own a.prefetch_owned
+// turns after the one it copies into shared memory (default 2: 16 chunks,
+// ~384 KB per SM, ~57 MB across 148 SMs), so HBM keeps streaming while warps
+// wait for activations.
+constexpr uint32_t kPollLimit = 1u << 21;  // polls of one flag-carrying word or of the step barrier
 
 struct __align__(128) Smem {
     uint8_t ring[kRingStages][kStageBytes];
-    half xs[kHidden];
+    half xs[kHidden];    // normalised activation of the current phase
+    half xraw[kHidden];  // residual stream entering the current phase
     half act[kMaxIM];
     float so[kConsumerWarps][kHeadDim];
+    half qkv_new[3][kHeadDim];  // attention: q, k and v of the new row for this CTA's head
     float sm[kConsumerWarps], sl[kConsumerWarps];
     float red[32];
     unsigned long long wkey[kConsumerWarps];
-    uint64_t full[kRingStages], empty[kRingStages];
-    volatile int stop;  // consumers -> producer: stop streaming and drain
-    volatile int fail;  // consumer-side failure broadcast
+    uint64_t full[kRingStages];
+    LayerPtrs layers[kMaxLayers];  // copy of a.layers (read at every phase change)
+    int range[5][4];               // per phase (qkv, o, w12, c, lm): this CTA's units [u0, u1), units per chunk, K
+    volatile int fail;  // a consumer wait expired
     int token;
     int last;
 };
@@ -49,53 +60,10 @@ __device__ __forceinline__ int chunk_units(int K) {
     return u < 1 ? 1 : u;
 }
 
-__device__ void record_error(DecodeControl* ctl, int code, int where) {
-    if (atomicCAS(&ctl->err, 0, code) == 0) ctl->err_where = where;
-}
-
-// ------------------------------------------------------------------ producer
-__device__ bool stream_phase(const half* W, int U, int K, uint32_t& chunk, Smem& s, uint64_t pol) {
-    const int b = blockIdx.x, G = gridDim.x;
-    const int u0 = (int)((long long)U * b / G), u1 = (int)((long long)U * (b + 1) / G);
-    const int CH = chunk_units(K);
-    for (int cu = u0; cu < u1; cu += CH) {
-        const int nun = (u1 - cu) < CH ? (u1 - cu) : CH;
-        const int slot = chunk & (kRingStages - 1);
-        if (chunk >= (uint32_t)kRingStages) {
-            if (!mbar_wait(&s.empty[slot], ((chunk >> 3) - 1) & 1, &s.stop)) return false;
-        }
-        const uint32_t bytes = (uint32_t)nun * 4u * (uint32_t)K;
-        mbar_arrive_expect_tx(&s.full[slot], bytes);
-        bulk_g2s(s.ring[slot], W + (size_t)cu * 2 * K, bytes, &s.full[slot], pol);
-        ++chunk;
-    }
-    return true;
-}
-
-__device__ void producer(const DecodeArgs& a, Smem& s) {
-    const uint64_t pol = l2_policy_evict_first();
-    uint32_t chunk = 0;
-    bool ok = true;
-    for (int step = 0; step < a.n_steps && ok; ++step) {
-        for (int l = 0; l < a.NL && ok; ++l) {
-            const LayerPtrs L = a.layers[l];
-            ok = stream_phase(L.qkv_w, 3 * kHidden / 2, kHidden, chunk, s, pol) &&
-                 stream_phase(L.proj_w, kHidden / 2, kHidden, chunk, s, pol) &&
-                 stream_phase(L.w12, a.IM, kHidden, chunk, s, pol) &&
-                 stream_phase(L.cproj, kHidden / 2, a.IM, chunk, s, pol);
-        }
-        if (ok && !a.skip_lm) ok = stream_phase(a.lm_head, a.V / 2, kHidden, chunk, s, pol);
-    }
-    // Drain: wait until every copy this CTA issued has landed before exiting.
-    for (int slot = 0; slot < kRingStages; ++slot) {
-        if (chunk > (uint32_t)slot) {
-            const uint32_t c = slot + 8u * ((chunk - 1u - slot) / 8u);
-            mbar_wait(&s.full[slot], (c >> 3) & 1);
-        }
-    }
-}
-
-// ------------------------------------------------------------------ consumers
+// fp32 FMA dot products of two weight rows (a unit) against the activation:
+// K = 2048 with the lane's 64-element activation slice in registers, or any
+// K with the activation in shared memory.  After the butterfly every lane
+// holds both sums.
 __device__ __forceinline__ void dot2_regs(const half* r0, const half* r1, const float* xr, int lane, float& s0,
                                           float& s1) {
     float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
@@ -152,55 +120,193 @@ __device__ __forceinline__ void dot2_smem(const half* r0, const half* r1, const 
     }
 }
 
+__device__ void record_error(DecodeControl* ctl, int code, int where) {
+    if (atomicCAS(&ctl->err, 0, code) == 0) ctl->err_where = where;
+}
+
+// ------------------------------------------------------------------ flag-carrying words
+__device__ __forceinline__ void ll_store(unsigned long long* p, uint32_t data, uint32_t tag) {
+    const unsigned long long v = ((unsigned long long)tag << 32) | data;
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_load(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Read N words p[i*stride] that must carry `tag`; data to out[i].  Returns
+// false when the words did not arrive within the poll bound.
+template <int N>
+__device__ __forceinline__ bool ll_read(const unsigned long long* p, int stride, uint32_t tag, uint32_t* out) {
+    uint32_t pending = (N == 32) ? 0xffffffffu : ((1u << N) - 1u);
+    for (uint32_t it = 0; it < kPollLimit; ++it) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            if (pending & (1u << i)) {
+                const unsigned long long v = ll_load(p + (size_t)i * stride);
+                if ((uint32_t)(v >> 32) == tag) {
+                    out[i] = (uint32_t)v;
+                    pending &= ~(1u << i);
+                }
+            }
+        }
+        if (!pending) return true;
+        __nanosleep(it < 8 ? 32 : 128);
+    }
+    return false;
+}
+
+// Timing probe (development aid, off when a.prof is null): thread 0 of each
+// CTA stamps %globaltimer at consecutive indices of its row of a.prof.
+__device__ __forceinline__ void probe(const DecodeArgs& a, int tid, int& np) {
+    if (a.prof && tid == 0) {
+        if (np < a.prof_cap) a.prof[((size_t)blockIdx.x * a.prof_cap + np) * 2] = globaltimer();
+        ++np;
+    }
+}
+
+struct Tags {
+    uint32_t base;
+    int NL;
+    __device__ __forceinline__ uint32_t operator()(int step, int layer, int slot) const {
+        return base + (uint32_t)((step * NL + layer) * LL_PER_LAYER + slot) + 1u;
+    }
+};
+
+// ------------------------------------------------------------------ weight feed
+// Walks this CTA's chunk sequence: per step, per layer the chunks of qkv_w,
+// proj_w, w12, cproj, then (unless skip_lm) lm_head.  Chunk i of the
+// sequence goes to ring slot i % 8.
+struct Feed {
+    int step, layer, phase;  // phase 0..3 = qkv, o, w12, c; 4 = lm_head
+    int cu, u1, CH, K;       // current unit, end of this CTA's range, units per chunk, row length
+    const half* W;
+    uint32_t chunk;          // sequence index of the current position
+    bool done;
+};
+
+__device__ __forceinline__ void feed_enter_phase(const DecodeArgs& a, const Smem& s, Feed& f) {
+    // move to the first non-empty phase at or after (step, layer, phase)
+    for (;;) {
+        if (f.step >= a.n_steps) { f.done = true; return; }
+        const half* W;
+        if (f.phase == 4) {
+            W = a.lm_head;
+        } else {
+            const LayerPtrs& L = s.layers[f.layer];
+            W = f.phase == 0 ? L.qkv_w : f.phase == 1 ? L.proj_w : f.phase == 2 ? L.w12 : L.cproj;
+        }
+        const int K = s.range[f.phase][3];
+        f.cu = s.range[f.phase][0];
+        f.u1 = s.range[f.phase][1];
+        f.CH = s.range[f.phase][2];
+        f.K = K;
+        f.W = W;
+        if (f.cu < f.u1) return;
+        // empty range: next phase
+        if (f.phase == 4 || (f.phase == 3 && f.layer == a.NL - 1)) {
+            if (f.phase == 3 && !a.skip_lm) { f.phase = 4; continue; }
+            f.step++; f.layer = 0; f.phase = 0;
+        } else if (f.phase == 3) {
+            f.layer++; f.phase = 0;
+        } else {
+            f.phase++;
+        }
+    }
+}
+
+__device__ __forceinline__ void feed_advance(const DecodeArgs& a, const Smem& s, Feed& f) {
+    f.cu += f.CH;
+    f.chunk++;
+    if (f.cu < f.u1) return;
+    if (f.phase == 4 || (f.phase == 3 && f.layer == a.NL - 1)) {
+        if (f.phase == 3 && !a.skip_lm) f.phase = 4;
+        else { f.step++; f.layer = 0; f.phase = 0; }
+    } else if (f.phase == 3) {
+        f.layer++; f.phase = 0;
+    } else {
+        f.phase++;
+    }
+    feed_enter_phase(a, s, f);
+}
+
+// Issue the copy of the next chunk owned by `warp` (lane 0 only).
+__device__ __forceinline__ void feed_issue_next(const DecodeArgs& a, Feed& f, Smem& s, int warp, uint64_t pol) {
+    while (!f.done && (int)(f.chunk & (kRingStages - 1)) != warp) feed_advance(a, s, f);
+    if (f.done) return;
+    const int nun = (f.u1 - f.cu) < f.CH ? (f.u1 - f.cu) : f.CH;
+    const uint32_t bytes = (uint32_t)nun * 4u * (uint32_t)f.K;
+    mbar_arrive_expect_tx(&s.full[warp], bytes);
+    bulk_g2s(s.ring[warp], f.W + (size_t)f.cu * 2 * f.K, bytes, &s.full[warp], pol);
+    feed_advance(a, s, f);
+}
+
+// L2 prefetch of the next chunk owned by `warp` on a second cursor.
+__device__ __forceinline__ void feed_prefetch_next(const DecodeArgs& a, const Smem& s, Feed& f, int warp) {
+    while (!f.done && (int)(f.chunk & (kRingStages - 1)) != warp) feed_advance(a, s, f);
+    if (f.done) return;
+    const int nun = (f.u1 - f.cu) < f.CH ? (f.u1 - f.cu) : f.CH;
+    bulk_prefetch_l2(f.W + (size_t)f.cu * 2 * f.K, (uint32_t)nun * 4u * (uint32_t)f.K);
+    feed_advance(a, s, f);
+}
+
+// ------------------------------------------------------------------ consumers
 struct StepCtx {
-    int pos, step;
+    int pos, step, layer;
     half* kcl;
     half* vcl;
     const half* bias;
     int ipt;
-    unsigned long long best;  // lane 0 of each warp: best argmax key seen in the LM phase
+    uint32_t tag;             // tag of the words the current phase writes
+    unsigned long long best;  // lane u of each warp: best argmax key of its units in the LM phase
 };
 
-// Grid-wide barrier over all CTAs (called by the 256 consumer threads).  The
-// named barriers always run, so a failure anywhere in the CTA never leaves a
-// consumer warp waiting on bar.sync; the global spin gives up when the count
-// does not arrive within the bound or when another CTA has recorded an error.
-__device__ bool grid_sync(const DecodeArgs& a, Smem& s, uint32_t& nbar, int tid, int where) {
-    named_bar_sync(1, 256);
+// The one grid-wide barrier of a step (publishes the argmax, orders KV rows).
+__device__ bool grid_sync(const DecodeArgs& a, Smem& s, uint32_t& nbar, int tid, bool bad, int& np) {
+    const bool any_bad = named_bar_or(1, 256, bad);
     ++nbar;
-    bool failed = false;
+    bool failed = any_bad;
+    probe(a, tid, np);
     if (tid == 0) {
-        __threadfence();
         red_release_gpu_add(&a.ctl->bar, 1u);
-        failed = s.fail != 0;
         if (!failed) {
             const uint32_t target = nbar * gridDim.x;
             bool ok = false;
-            for (uint32_t i = 0; i < kSpinLimit; ++i) {
+            for (uint32_t i = 0; i < kPollLimit; ++i) {
                 if (ld_acquire_gpu(&a.ctl->bar) >= target) { ok = true; break; }
                 if ((i & 63) == 63 && *(volatile int*)&a.ctl->err != 0) break;
-                if (i > 512) __nanosleep(32);
+                if (i > 256) __nanosleep(32);
             }
             if (!ok) {
-                record_error(a.ctl, kErrGridBarrierTimeout, where);
-                s.fail = 1;
+                record_error(a.ctl, kErrGridBarrierTimeout, PH_LM);
                 failed = true;
             }
         }
-        __threadfence();
     }
+    probe(a, tid, np);
     // every consumer thread gets the same verdict, so later branches stay CTA-uniform
     return !named_bar_or(1, 256, failed);
 }
 
-// Stage x (global) in shared memory, RMSNorm it with the reference tree, and
-// leave each lane's 64-element slice of the normalised vector in xr.
-__device__ void load_norm(const half* src, bool written_this_launch, const half* w, half* copy_out, Smem& s,
-                          int tid, float* xr) {
-    const uint4 v = written_this_launch ? ld_cg_u4(src + tid * 8) : *reinterpret_cast<const uint4*>(src + tid * 8);
-    *reinterpret_cast<uint4*>(s.xs + tid * 8) = v;
-    if (copy_out) *reinterpret_cast<uint4*>(copy_out + tid * 8) = v;
-    const float r = rms_scale_tree256(s.xs, kHidden, 1e-6f, s.red, tid, 1);
+// Stage a residual-stream vector in shared memory (raw copy in xraw),
+// RMSNorm it with the reference tree and leave each lane's 64-element slice
+// of the normalised vector in xr.  The source is either a plain fp16 row (the
+// embedding) or flag-carrying words with `tag`.  Returns the CTA-wide failure
+// verdict (true = a wait expired somewhere in the CTA).
+__device__ bool load_norm(const half* plain, const unsigned long long* ll, uint32_t tag, const half* w, Smem& s,
+                          int tid, float* xr, bool bad) {
+    uint4 v;
+    if (plain) {
+        v = *reinterpret_cast<const uint4*>(plain + tid * 8);
+    } else {
+        uint32_t d[4];
+        bad |= !ll_read<4>(ll + tid * 4, 1, tag, d);
+        v = make_uint4(d[0], d[1], d[2], d[3]);
+    }
+    // the previous phase may still read xraw / xs: wait before overwriting
+    if (named_bar_or(1, 256, bad)) return true;
+    *reinterpret_cast<uint4*>(s.xraw + tid * 8) = v;
+    const float r = rms_scale_tree256(s.xraw, kHidden, 1e-6f, s.red, tid, 1);
     float xf[8], wf[8], of[8];
     unpack8(v, xf);
     unpack8(*reinterpret_cast<const uint4*>(w + tid * 8), wf);
@@ -211,43 +317,50 @@ __device__ void load_norm(const half* src, bool written_this_launch, const half*
     const int lane = tid & 31;
 #pragma unroll
     for (int j = 0; j < 8; ++j) unpack8(*reinterpret_cast<const uint4*>(s.xs + 256 * j + 8 * lane), xr + 8 * j);
+    return false;
 }
 
 template <int PH>
-__device__ __forceinline__ void epilogue(const DecodeArgs& a, StepCtx& c, int u, float s0, float s1) {
+__device__ __forceinline__ void epilogue(const DecodeArgs& a, const Smem& s, StepCtx& c, int u, float s0, float s1,
+                                         float bias0, float bias1) {
     if constexpr (PH == PH_QKV) {
         const int sec = u / (kHidden / 2), v = u % (kHidden / 2), h = v / 64, t = v % 64;
-        const int i1 = sec * kHidden + h * kHeadDim + t, i2 = i1 + 64;
-        const float y1 = h2f(f2h(h2f(f2h(s0)) + h2f(c.bias[i1])));
-        const float y2 = h2f(f2h(h2f(f2h(s1)) + h2f(c.bias[i2])));
+        const float y1 = h2f(f2h(h2f(f2h(s0)) + bias0));
+        const float y2 = h2f(f2h(h2f(f2h(s1)) + bias1));
         const int o1 = h * kHeadDim + t, o2 = o1 + 64;
         const size_t row = (size_t)c.pos * kHidden;
+        half r1, r2;
         if (sec == 2) {
-            c.vcl[row + o1] = f2h(y1);
-            c.vcl[row + o2] = f2h(y2);
+            r1 = f2h(y1);
+            r2 = f2h(y2);
+            c.vcl[row + o1] = r1;
+            c.vcl[row + o2] = r2;
         } else {
             // fused_qkv_rope_cache.cuh:36-43 with the fast-math intrinsics
             const float theta = (float)c.pos * __powf(10000.0f, __fdividef(-2.0f * (float)t, (float)kHeadDim));
             const float cs = __cosf(theta), sn = __sinf(theta);
-            const half r1 = f2h(y1 * cs - y2 * sn);
-            const half r2 = f2h(y2 * cs + y1 * sn);
-            if (sec == 0) {
-                a.q[o1] = r1;
-                a.q[o2] = r2;
-            } else {
+            r1 = f2h(y1 * cs - y2 * sn);
+            r2 = f2h(y2 * cs + y1 * sn);
+            if (sec == 1) {
                 c.kcl[row + o1] = r1;
                 c.kcl[row + o2] = r2;
             }
         }
+        ll_store(a.ll_qkv + u, (uint32_t)__half_as_ushort(r1) | ((uint32_t)__half_as_ushort(r2) << 16), c.tag);
     } else if constexpr (PH == PH_O || PH == PH_C) {
         const int n = 2 * u;
-        const half2 xo = __halves2half2(__ushort_as_half(ld_cg_u16(a.x + n)), __ushort_as_half(ld_cg_u16(a.x + n + 1)));
-        const float r0 = h2f(__low2half(xo)) + h2f(f2h(s0));
-        const float r1 = h2f(__high2half(xo)) + h2f(f2h(s1));
-        *reinterpret_cast<half2*>(a.x + n) = __floats2half2_rn(r0, r1);
+        const half2 xo = *reinterpret_cast<const half2*>(s.xraw + n);
+        const half2 r = __floats2half2_rn(h2f(__low2half(xo)) + h2f(f2h(s0)), h2f(__high2half(xo)) + h2f(f2h(s1)));
+        const uint32_t bits = *reinterpret_cast<const uint32_t*>(&r);
+        if constexpr (PH == PH_O) {
+            ll_store(a.ll_xo + u, bits, c.tag);
+        } else {
+            ll_store(a.ll_xc + u, bits, c.tag);
+            if (c.layer == a.NL - 1) *reinterpret_cast<half2*>(a.x + n) = r;
+        }
     } else if constexpr (PH == PH_W12) {
         const float g = h2f(f2h(s0)), up = h2f(f2h(s1));
-        a.act[u] = f2h(g * __fdividef(up, 1.0f + __expf(-up)));
+        ll_store(a.ll_act + u, (uint32_t)__half_as_ushort(f2h(g * __fdividef(up, 1.0f + __expf(-up)))), c.tag);
     } else if constexpr (PH == PH_LM) {
         const int n = 2 * u;
         const half l0 = f2h(s0), l1 = f2h(s1);
@@ -259,59 +372,138 @@ __device__ __forceinline__ void epilogue(const DecodeArgs& a, StepCtx& c, int u,
     }
 }
 
+// Consume this CTA's chunks of one weight matrix (rows in units of two).
+// A wait that expires marks `bad` and the remaining chunks are skipped.
 template <int PH, bool kRegs>
-__device__ void gemv_phase(const DecodeArgs& a, Smem& s, StepCtx& c, int U, int K, uint32_t& chunk, const float* xr,
-                           int warp, int lane) {
-    const int b = blockIdx.x, G = gridDim.x;
-    const int u0 = (int)((long long)U * b / G), u1 = (int)((long long)U * (b + 1) / G);
-    const int CH = chunk_units(K);
+__device__ void gemv_phase(const DecodeArgs& a, Smem& s, StepCtx& c, int K, uint32_t& chunk, const float* xr,
+                           int warp, int lane, bool& bad, Feed& feed, Feed& pre, uint64_t pol) {
+    constexpr int R = PH == PH_QKV ? 0 : PH == PH_O ? 1 : PH == PH_W12 ? 2 : PH == PH_C ? 3 : 4;
+    const int u0 = s.range[R][0], u1 = s.range[R][1], CH = s.range[R][2];
+    unsigned long long pw = 0, pc = 0, pi = 0, pn = 0;  // probe sums (profiling only)
     for (int cu = u0; cu < u1; cu += CH, ++chunk) {
         if ((int)(chunk & (kRingStages - 1)) != warp) continue;
         const int nun = (u1 - cu) < CH ? (u1 - cu) : CH;
-        if (s.fail) continue;
+        if (bad || s.fail) continue;
+        const unsigned long long t0 = a.prof_prod ? (unsigned long long)clock64() : 0ull;
         if (!mbar_wait(&s.full[warp], (chunk >> 3) & 1, &s.fail)) {
             if (lane == 0) record_error(a.ctl, kErrRingTimeout, PH);
             s.fail = 1;
+            bad = true;
             continue;
         }
-        const half* buf = reinterpret_cast<const half*>(s.ring[warp]);
-        for (int j = 0; j < nun; ++j) {
-            const half* r0 = buf + (size_t)j * 2 * K;
-            float s0, s1;
-            if constexpr (kRegs) dot2_regs(r0, r0 + K, xr, lane, s0, s1);
-            else dot2_smem(r0, r0 + K, s.act, K, lane, s0, s1);
-            if (lane == 0) epilogue<PH>(a, c, cu + j, s0, s1);
+        const unsigned long long t1 = a.prof_prod ? (unsigned long long)clock64() : 0ull;
+        // QKV: the bias pair of unit `lane` is fetched before the dot products
+        float b0 = 0.f, b1 = 0.f;
+        if constexpr (PH == PH_QKV) {
+            if (lane < nun) {
+                const int u = cu + lane, sec = u / (kHidden / 2), v = u % (kHidden / 2);
+                const int i1 = sec * kHidden + (v / 64) * kHeadDim + (v % 64);
+                b0 = h2f(c.bias[i1]);
+                b1 = h2f(c.bias[i1 + 64]);
+            }
         }
+        const half* buf = reinterpret_cast<const half*>(s.ring[warp]);
+        float r0s = 0.f, r1s = 0.f;  // lane j keeps unit j's two dot products
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            if (j < nun) {
+                const half* r0 = buf + (size_t)j * 2 * K;
+                float s0, s1;
+                if constexpr (kRegs) dot2_regs(r0, r0 + K, xr, lane, s0, s1);
+                else dot2_smem(r0, r0 + K, s.act, K, lane, s0, s1);
+                if (lane == j) { r0s = s0; r1s = s1; }
+            }
+        }
+        if (lane < nun) epilogue<PH>(a, s, c, cu + lane, r0s, r1s, b0, b1);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s.empty[warp]);
+        const unsigned long long t2 = a.prof_prod ? (unsigned long long)clock64() : 0ull;
+        // the slot is drained: stream this warp's next chunk into it, and
+        // prefetch into L2 the one a.prefetch_owned turns further on
+        if (lane == 0) {
+            feed_issue_next(a, feed, s, warp, pol);
+            if (a.prefetch_owned > 0) feed_prefetch_next(a, s, pre, warp);
+        }
+        if (a.prof_prod) {
+            pw += t1 - t0;
+            pc += t2 - t1;
+            pi += (unsigned long long)clock64() - t2;
+            pn += 1;
+        }
+    }
+    if (a.prof_prod && lane == 0 && pn) {
+        // per CTA, phase and warp: SM cycles waiting for chunks, computing, issuing; chunks
+        unsigned long long* q = a.prof_prod + (((size_t)blockIdx.x * 6 + PH) * kConsumerWarps + warp) * 4;
+        q[0] += pw;
+        q[1] += pc;
+        q[2] += pi;
+        q[3] += pn;
     }
 }
 
 // Split-KV attention of one (head, split) per CTA; the last CTA to finish a
-// head merges the 9 partials into att[h*128 .. +128] (fp16).
-__device__ void attention_phase(const DecodeArgs& a, Smem& s, const StepCtx& c, int tid) {
+// head merges the 9 partials and publishes att for that head.  Rows < pos
+// come from the KV cache (written by earlier steps, ordered by the step
+// barrier); the query and the new row pos come from the QKV phase's words.
+// Returns the CTA-wide failure verdict.
+__device__ bool attention_phase(const DecodeArgs& a, Smem& s, const StepCtx& c, const Tags& tags, int tid,
+                                bool bad) {
     const int b = blockIdx.x;
     constexpr int S = kAttnSplits;
-    if (b >= kHeads * S) return;
-    const int h = b / S, sp = b % S, L = c.pos + 1;
+    const bool active = b < kHeads * S;
+    const int h = active ? b / S : 0, sp = active ? b % S : 0, L = c.pos + 1;
     const int warp = tid >> 5, lane = tid & 31, dl = (lane & 15) * 8;
     const int r0 = (int)((long long)L * sp / S), r1 = (int)((long long)L * (sp + 1) / S);
-    const int n = r1 - r0;
-    const int w0 = r0 + n * warp / 8, w1 = r0 + n * (warp + 1) / 8;
-    float q8[8];
-    unpack8(ld_cg_u4(a.q + h * kHeadDim + dl), q8);
-    const float scale = __frcp_rn(sqrtf((float)kHeadDim));
-    float m = -INFINITY, l = 0.f, o8[8];
+    const bool has_new = active && r0 < L && r1 == L;  // this split owns row pos
+    const uint32_t tq = tags(c.step, c.layer, LL_QKV);
+    float q8[8], m = -INFINITY, l = 0.f, o8[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) o8[e] = 0.f;
-    if (w0 < w1) attend_rows<true>(c.kcl + h * kHeadDim, c.vcl + h * kHeadDim, kHidden, w0, w1, q8, scale, m, l, o8);
-    combine_halfwarps(m, l, o8);
-    if (lane < 16) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) s.so[warp][dl + e] = o8[e];
+    // Each word is polled by one thread: threads 0..63 the query, 64..191 the
+    // new row's k and v (only the split that owns row pos needs them).
+    if (active && (tid < 64 || (has_new && tid < 192))) {
+        const int sec = tid >> 6, t = tid & 63;
+        uint32_t w[1] = {0};
+        bad |= !ll_read<1>(a.ll_qkv + sec * (kHidden / 2) + h * 64 + t, 1, tq, w);
+        s.qkv_new[sec][t] = __ushort_as_half((uint16_t)(w[0] & 0xffffu));
+        s.qkv_new[sec][t + 64] = __ushort_as_half((uint16_t)(w[0] >> 16));
     }
-    if (lane == 0) { s.sm[warp] = m; s.sl[warp] = l; }
-    named_bar_sync(1, 256);
+    if (named_bar_or(1, 256, bad)) return true;
+    if (active) {
+        unpack8(*reinterpret_cast<const uint4*>(&s.qkv_new[0][dl]), q8);
+        const float scale = __frcp_rn(sqrtf((float)kHeadDim));
+        const int rend = has_new ? L - 1 : r1;  // rows from the cache
+        const int n = rend - r0;
+        const int w0 = r0 + n * warp / 8, w1 = r0 + n * (warp + 1) / 8;
+        if (w0 < w1)
+            attend_rows<true>(c.kcl + h * kHeadDim, c.vcl + h * kHeadDim, kHidden, w0, w1, q8, scale, m, l, o8);
+        combine_halfwarps(m, l, o8);
+        if (has_new && warp == 0) {
+            // row pos from the QKV phase's words
+            float kf[8], vf[8];
+            unpack8(*reinterpret_cast<const uint4*>(&s.qkv_new[1][dl]), kf);
+            unpack8(*reinterpret_cast<const uint4*>(&s.qkv_new[2][dl]), vf);
+            float d = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) d = __fmaf_rn(q8[e], kf[e], d);
+#pragma unroll
+            for (int mk = 8; mk >= 1; mk >>= 1) d += __shfl_xor_sync(0xffffffffu, d, mk);
+            const float sc = d * scale;
+            const float mx = fmaxf(m, sc);
+            const float corr = (m == -INFINITY) ? 0.f : __expf(m - mx);
+            const float p = __expf(sc - mx);
+            l = l * corr + p;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o8[e] = __fmaf_rn(p, vf[e], o8[e] * corr);
+            m = mx;
+        }
+        if (lane < 16) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s.so[warp][dl + e] = o8[e];
+        }
+        if (lane == 0) { s.sm[warp] = m; s.sl[warp] = l; }
+    }
+    if (named_bar_or(1, 256, bad)) return true;
+    if (!active) return false;
     float* part = a.att_part + (size_t)(h * S + sp) * 130;
     if (tid < kHeadDim) {
         float M = -INFINITY;
@@ -334,73 +526,127 @@ __device__ void attention_phase(const DecodeArgs& a, Smem& s, const StepCtx& c, 
         __threadfence();
     }
     named_bar_sync(1, 256);
-    if (s.last && tid < kHeadDim) {
+    if (s.last && tid < kHeadDim / 2) {
+        // merge; thread j produces dims (2j, 2j+1) of head h as one word
         const float* base = a.att_part + (size_t)h * S * 130;
         float M = -INFINITY;
         for (int j = 0; j < S; ++j) M = fmaxf(M, __ldcg(base + j * 130 + 128));
-        float Ls = 0.f, acc = 0.f;
+        float Ls = 0.f, acc0 = 0.f, acc1 = 0.f;
         for (int j = 0; j < S; ++j) {
             const float mj = __ldcg(base + j * 130 + 128);
             if (mj == -INFINITY) continue;
             const float f = __expf(mj - M);
             Ls += __ldcg(base + j * 130 + 129) * f;
-            acc += __ldcg(base + j * 130 + tid) * f;
+            acc0 += __ldcg(base + j * 130 + 2 * tid) * f;
+            acc1 += __ldcg(base + j * 130 + 2 * tid + 1) * f;
         }
-        a.att[h * kHeadDim + tid] = f2h(acc * __frcp_rn(Ls));
+        const float inv = __frcp_rn(Ls);
+        const half2 r = __floats2half2_rn(acc0 * inv, acc1 * inv);
+        ll_store(a.ll_att + h * 64 + tid, *reinterpret_cast<const uint32_t*>(&r), tags(c.step, c.layer, LL_ATT));
     }
+    return false;
 }
 
 __device__ void consumers(const DecodeArgs& a, Smem& s) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint32_t chunk = 0, nbar = 0;
     int token = a.first_token;
-    float xr[64];
     StepCtx c;
+    float xr[64];
     c.ipt = (a.V + 511) / 512;
+    const Tags tags{a.flag_base, a.NL};
+    bool bad = false;
+    int np = 0;  // probe index (thread 0)
+    const uint64_t pol = l2_policy_evict_first();
+    Feed feed{};
+    feed.step = 0; feed.layer = 0; feed.phase = 0; feed.chunk = 0; feed.done = false;
+    Feed pre = feed;
+    if (lane == 0) {
+        feed_enter_phase(a, s, feed);
+        feed_issue_next(a, feed, s, warp, pol);  // this warp's first chunk
+        pre = feed;                              // L2 prefetch cursor starts at the next owned chunk
+        for (int i = 0; i < a.prefetch_owned; ++i) feed_prefetch_next(a, s, pre, warp);
+    }
     for (int step = 0; step < a.n_steps; ++step) {
         c.pos = a.pos0 + step;
         c.step = step;
         const half* emb = a.wte + (size_t)token * kHidden;
-        bool ok = true;
-        for (int l = 0; l < a.NL && ok; ++l) {
-            const LayerPtrs L = a.layers[l];
+        bool failed = false;
+        for (int l = 0; l < a.NL; ++l) {
+            const LayerPtrs& L = s.layers[l];
+            c.layer = l;
             c.kcl = a.kc + (size_t)l * a.max_seqlen * kHidden;
             c.vcl = a.vc + (size_t)l * a.max_seqlen * kHidden;
             c.bias = L.qkv_b;
             // QKV (qwen_infer.cu:626-642)
-            if (l == 0) load_norm(emb, false, L.ln1, blockIdx.x == 0 ? a.x : nullptr, s, tid, xr);
-            else load_norm(a.x, true, L.ln1, nullptr, s, tid, xr);
-            gemv_phase<PH_QKV, true>(a, s, c, 3 * kHidden / 2, kHidden, chunk, xr, warp, lane);
-            if (!grid_sync(a, s, nbar, tid, PH_QKV)) { ok = false; break; }
+            probe(a, tid, np);
+            failed = (l == 0) ? load_norm(emb, nullptr, 0, L.ln1, s, tid, xr, bad)
+                              : load_norm(nullptr, a.ll_xc, tags(step, l - 1, LL_XC), L.ln1, s, tid, xr, bad);
+            if (failed) break;
+            c.tag = tags(step, l, LL_QKV);
+            probe(a, tid, np);
+            gemv_phase<PH_QKV, true>(a, s, c, kHidden, chunk, xr, warp, lane, bad, feed, pre, pol);
             // attention (qwen_infer.cu:646-677)
-            attention_phase(a, s, c, tid);
-            if (!grid_sync(a, s, nbar, tid, PH_ATT)) { ok = false; break; }
-            // o_proj + residual (qwen_infer.cu:701-704)
+            probe(a, tid, np);
+            failed = attention_phase(a, s, c, tags, tid, bad);
+            if (failed) break;
+            probe(a, tid, np);
+            // o_proj + residual (qwen_infer.cu:701-704): each thread polls its own
+            // four words of att into shared memory, then every warp takes its slice
+            {
+                uint32_t d[4];
+                bad |= !ll_read<4>(a.ll_att + 4 * tid, 1, tags(step, l, LL_ATT), d);
+                failed = named_bar_or(1, 256, bad);  // the previous phase is done with s.xs
+                if (failed) break;
+                *reinterpret_cast<uint4*>(s.xs + 8 * tid) = make_uint4(d[0], d[1], d[2], d[3]);
+                named_bar_sync(1, 256);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) unpack8(ld_cg_u4(a.att + 256 * j + 8 * lane), xr + 8 * j);
-            gemv_phase<PH_O, true>(a, s, c, kHidden / 2, kHidden, chunk, xr, warp, lane);
-            if (!grid_sync(a, s, nbar, tid, PH_O)) { ok = false; break; }
+                for (int j = 0; j < 8; ++j)
+                    unpack8(*reinterpret_cast<const uint4*>(s.xs + 256 * j + 8 * lane), xr + 8 * j);
+            }
+            c.tag = tags(step, l, LL_XO);
+            probe(a, tid, np);
+            gemv_phase<PH_O, true>(a, s, c, kHidden, chunk, xr, warp, lane, bad, feed, pre, pol);
             // RMSNorm + w1/w2 + SwiGLU (qwen_infer.cu:708-715)
-            load_norm(a.x, true, L.ln2, nullptr, s, tid, xr);
-            gemv_phase<PH_W12, true>(a, s, c, a.IM, kHidden, chunk, xr, warp, lane);
-            if (!grid_sync(a, s, nbar, tid, PH_W12)) { ok = false; break; }
-            // c_proj + residual (qwen_infer.cu:718-721)
-            for (int i = tid * 8; i < a.IM; i += 256 * 8)
-                *reinterpret_cast<uint4*>(s.act + i) = ld_cg_u4(a.act + i);
-            named_bar_sync(1, 256);
-            gemv_phase<PH_C, false>(a, s, c, kHidden / 2, a.IM, chunk, xr, warp, lane);
-            if (!grid_sync(a, s, nbar, tid, PH_C)) { ok = false; break; }
+            probe(a, tid, np);
+            failed = load_norm(nullptr, a.ll_xo, tags(step, l, LL_XO), L.ln2, s, tid, xr, bad);
+            if (failed) break;
+            c.tag = tags(step, l, LL_ACT);
+            probe(a, tid, np);
+            gemv_phase<PH_W12, true>(a, s, c, kHidden, chunk, xr, warp, lane, bad, feed, pre, pol);
+            probe(a, tid, np);
+            // c_proj + residual (qwen_infer.cu:718-721).  s.act was last read by the
+            // previous layer's C phase, which every warp has left (several named
+            // barriers since), so the words go straight to shared memory.
+            {
+                const uint32_t ta = tags(step, l, LL_ACT);
+                for (int i = tid; i < a.IM; i += 256) {
+                    uint32_t d[1] = {0};
+                    bad |= !ll_read<1>(a.ll_act + i, 1, ta, d);
+                    s.act[i] = __ushort_as_half((uint16_t)d[0]);
+                }
+                failed = named_bar_or(1, 256, bad);
+                if (failed) break;
+            }
+            c.tag = tags(step, l, LL_XC);
+            probe(a, tid, np);
+            gemv_phase<PH_C, false>(a, s, c, a.IM, chunk, xr, warp, lane, bad, feed, pre, pol);
         }
-        if (!ok) break;
+        if (failed) break;
         if (a.skip_lm) {
+            // prefill through the decode path: the step barrier orders this step's KV rows
+            if (!grid_sync(a, s, nbar, tid, bad, np)) break;
             if (step + 1 < a.n_steps) token = a.forced[step + 1];
             if (blockIdx.x == 0 && tid == 0) a.ctl->n_done = step + 1;
             continue;
         }
         // final RMSNorm + lm_head + argmax (qwen_infer.cu:725-731)
-        load_norm(a.x, true, a.lnf, nullptr, s, tid, xr);
+        probe(a, tid, np);
+        if (load_norm(nullptr, a.ll_xc, tags(step, a.NL - 1, LL_XC), a.lnf, s, tid, xr, bad)) break;
         c.best = 0ull;
-        gemv_phase<PH_LM, true>(a, s, c, a.V / 2, kHidden, chunk, xr, warp, lane);
+        probe(a, tid, np);
+        gemv_phase<PH_LM, true>(a, s, c, kHidden, chunk, xr, warp, lane, bad, feed, pre, pol);
+        c.best = warp_max_u64(c.best);  // lanes 0..2 each tracked their own units
         if (lane == 0) s.wkey[warp] = c.best;
         named_bar_sync(1, 256);
         if (tid == 0) {
@@ -408,7 +654,7 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
             for (int w = 0; w < kConsumerWarps; ++w) k = s.wkey[w] > k ? s.wkey[w] : k;
             if (k) atomicMax(&a.ctl->best[step & 1], k);
         }
-        if (!grid_sync(a, s, nbar, tid, PH_LM)) break;
+        if (!grid_sync(a, s, nbar, tid, bad, np)) break;
         if (tid == 0) {
             const unsigned long long k = atomicOr(&a.ctl->best[step & 1], 0ull);
             const int t = argmax_key_index(k);
@@ -432,32 +678,54 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
         }
         if (token == a.stop0 || token == a.stop1) break;
     }
-    if (tid == 0) s.stop = 1;
+    if (bad) record_error(a.ctl, kErrHeadMergeTimeout, -1);
+    // Drain: the last copy this warp issued must have landed before the CTA
+    // exits (waiting on an already-consumed chunk returns at once: no later
+    // copy went to this slot).
+    if (lane == 0 && feed.chunk > 0) {
+        uint32_t last = feed.chunk - 1;
+        const uint32_t r = (uint32_t)warp;
+        if ((last & 7u) >= r) last -= (last & 7u) - r;
+        else if (last >= 8u) last = last - (last & 7u) - 8u + r;
+        else last = 0xffffffffu;
+        if (last != 0xffffffffu) mbar_wait(&s.full[warp], (last >> 3) & 1);
+    }
 }
 
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>(smem_raw);
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kRingStages; ++i) {
-            mbar_init(&s.full[i], 1);
-            mbar_init(&s.empty[i], 1);
-        }
-        s.stop = 0;
+        for (int i = 0; i < kRingStages; ++i) mbar_init(&s.full[i], 1);
         s.fail = 0;
         mbar_fence_init();
     }
-    __syncthreads();
-    if (threadIdx.x >= kConsumerWarps * 32) {
-        if (threadIdx.x == kConsumerWarps * 32) producer(a, s);
-        return;
+    for (int i = threadIdx.x; i < a.NL * (int)(sizeof(LayerPtrs) / sizeof(uint64_t)); i += blockDim.x)
+        reinterpret_cast<uint64_t*>(s.layers)[i] = reinterpret_cast<const uint64_t*>(a.layers)[i];
+    if (threadIdx.x < 5) {
+        // this CTA's unit range of each phase: the same for every layer and step
+        const int ph = threadIdx.x;
+        const int U = ph == 0 ? 3 * kHidden / 2 : ph == 1 ? kHidden / 2 : ph == 2 ? a.IM : ph == 3 ? kHidden / 2 : a.V / 2;
+        const int K = ph == 3 ? a.IM : kHidden;
+        const int b = blockIdx.x, G = gridDim.x;
+        s.range[ph][0] = (int)((long long)U * b / G);
+        s.range[ph][1] = (int)((long long)U * (b + 1) / G);
+        s.range[ph][2] = chunk_units(K);
+        s.range[ph][3] = K;
     }
+    __syncthreads();
     consumers(a, s);
 }
 
 }  // namespace
 
 size_t decode_smem_bytes() { return sizeof(Smem); }
+
+// Number of flag tags one launch of n_steps consumes (the host advances its
+// running tag base by this much after every launch).
+uint32_t decode_tags_per_launch(int n_steps, int num_layers) {
+    return (uint32_t)(n_steps * num_layers * LL_PER_LAYER + 1);
+}
 
 cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t stream) {
     cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <thread>
@@ -25,6 +26,7 @@
 
 namespace llmdiy {
 size_t decode_smem_bytes();
+uint32_t decode_tags_per_launch(int n_steps, int num_layers);
 cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t stream);
 
 namespace {
@@ -75,8 +77,12 @@ struct llmdiy_engine {
     // state
     half* kc = nullptr;
     half* vc = nullptr;
-    half *x = nullptr, *q = nullptr, *att = nullptr, *act = nullptr, *logits = nullptr;
+    half *x = nullptr, *logits = nullptr;
     float* att_part = nullptr;
+    unsigned long long* ll = nullptr;  // flag-carrying words: qkv | att | xo | act | xc
+    size_t ll_words = 0;
+    uint32_t tag_base = 0;
+    int prefetch_owned = 0;  // L2 prefetch distance of the decode kernel (LLMDIY_L2_PREFETCH overrides)
     DecodeControl* ctl = nullptr;
     int* tokens_dev = nullptr;
     int* forced_dev = nullptr;
@@ -108,8 +114,10 @@ int cuda_fail(llmdiy_engine* e, cudaError_t c, const char* what) {
 int check_config(llmdiy_engine* e, const llmdiy_config& c) {
     if (c.hidden_size != (uint32_t)kHidden || c.num_heads != (uint32_t)kHeads)
         return fail(e, LLMDIY_ERR_UNSUPPORTED, "fused decode kernel is built for hidden_size 2048 / 16 heads x 128");
-    if (c.intermediate_size == 0 || c.intermediate_size % 8 || c.intermediate_size > 6144)
-        return fail(e, LLMDIY_ERR_UNSUPPORTED, "intermediate_size must be a multiple of 8 and <= 6144");
+    if (c.intermediate_size == 0 || c.intermediate_size % 32 || c.intermediate_size > 6144)
+        return fail(e, LLMDIY_ERR_UNSUPPORTED, "intermediate_size must be a multiple of 32 and <= 6144");
+    if (c.num_layers > (uint32_t)kMaxLayers)
+        return fail(e, LLMDIY_ERR_UNSUPPORTED, "at most 64 layers");
     if (c.vocab_size == 0 || c.vocab_size % 2 || c.num_layers == 0 || c.max_seqlen == 0)
         return fail(e, LLMDIY_ERR_UNSUPPORTED, "vocab_size must be even; layers and max_seqlen non-zero");
     return LLMDIY_OK;
@@ -235,9 +243,9 @@ int alloc_state(llmdiy_engine* e) {
     CK(cudaMalloc(&e->kc, kv * 2), "cudaMalloc K cache");
     CK(cudaMalloc(&e->vc, kv * 2), "cudaMalloc V cache");
     CK(cudaMalloc(&e->x, H * 2), "alloc x");
-    CK(cudaMalloc(&e->q, H * 2), "alloc q");
-    CK(cudaMalloc(&e->att, H * 2), "alloc att");
-    CK(cudaMalloc(&e->act, (size_t)c.intermediate_size * 2), "alloc act");
+    e->ll_words = 3 * H / 2 + H / 2 + H / 2 + c.intermediate_size + H / 2;
+    CK(cudaMalloc(&e->ll, e->ll_words * 8), "alloc flag words");
+    CK(cudaMemset(e->ll, 0, e->ll_words * 8), "clear flag words");
     CK(cudaMalloc(&e->logits, (size_t)c.vocab_size * 2), "alloc logits");
     CK(cudaMalloc(&e->att_part, sizeof(float) * kHeads * kAttnSplits * 130), "alloc partials");
     CK(cudaMalloc(&e->ctl, sizeof(DecodeControl)), "alloc control");
@@ -260,6 +268,7 @@ int create_common(llmdiy_engine* e, Source& src) {
     if (prop.sharedMemPerBlockOptin < decode_smem_bytes())
         return fail(e, LLMDIY_ERR_UNSUPPORTED, "not enough shared memory per block for the decode kernel");
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+    if (const char* pf = std::getenv("LLMDIY_L2_PREFETCH")) e->prefetch_owned = std::max(0, std::atoi(pf));
     int rc = load_weights(e, src);
     if (rc) return rc;
     return alloc_state(e);
@@ -267,7 +276,8 @@ int create_common(llmdiy_engine* e, Source& src) {
 
 // Launch the decode kernel for n_steps steps (first input token, first position).
 int launch(llmdiy_engine* e, int first_token, int pos0, int n_steps, bool skip_lm, bool stop_on_eos, bool stream_host,
-           cudaStream_t st) {
+           cudaStream_t st, unsigned long long* prof = nullptr, unsigned long long* prof_prod = nullptr,
+           int prof_cap = 0) {
     const llmdiy_config& c = e->cfg;
     if (n_steps <= 0) return LLMDIY_OK;
     if (pos0 < 0 || (long long)pos0 + n_steps > (long long)c.max_seqlen)
@@ -283,10 +293,22 @@ int launch(llmdiy_engine* e, int first_token, int pos0, int n_steps, bool skip_l
     a.kc = e->kc;
     a.vc = e->vc;
     a.x = e->x;
-    a.q = e->q;
-    a.att = e->att;
-    a.act = e->act;
     a.logits = e->logits;
+    const size_t H = c.hidden_size;
+    a.ll_qkv = e->ll;
+    a.ll_att = a.ll_qkv + 3 * H / 2;
+    a.ll_xo = a.ll_att + H / 2;
+    a.ll_act = a.ll_xo + H / 2;
+    a.ll_xc = a.ll_act + c.intermediate_size;
+    // tags are unique per phase instance across launches; on wrap-around the
+    // words are cleared so no stale word can carry a future tag
+    const uint32_t need = decode_tags_per_launch(n_steps, (int)c.num_layers);
+    if ((uint64_t)e->tag_base + need >= 0xFFFFFFF0ull) {
+        CK(cudaMemsetAsync(e->ll, 0, e->ll_words * 8, st), "clear flag words");
+        e->tag_base = 0;
+    }
+    a.flag_base = e->tag_base;
+    e->tag_base += need;
     a.att_part = e->att_part;
     a.ctl = e->ctl;
     a.tokens_out = e->tokens_dev;
@@ -303,6 +325,10 @@ int launch(llmdiy_engine* e, int first_token, int pos0, int n_steps, bool skip_l
     a.skip_lm = skip_lm ? 1 : 0;
     a.stop0 = stop_on_eos ? 151645 : -1;  // qwen_infer.cu:808
     a.stop1 = stop_on_eos ? 151643 : -1;
+    a.prefetch_owned = e->prefetch_owned;
+    a.prof = prof;
+    a.prof_prod = prof_prod;
+    a.prof_cap = prof_cap;
     CK(launch_decode(a, e->num_sms, st), "decode launch");
     e->last_steps = n_steps;
     return LLMDIY_OK;
@@ -396,9 +422,7 @@ void llmdiy_engine_destroy(llmdiy_engine* e) {
     cudaFree(e->kc);
     cudaFree(e->vc);
     cudaFree(e->x);
-    cudaFree(e->q);
-    cudaFree(e->att);
-    cudaFree(e->act);
+    cudaFree(e->ll);
     cudaFree(e->logits);
     cudaFree(e->att_part);
     cudaFree(e->ctl);
@@ -429,9 +453,6 @@ int llmdiy_engine_reset(llmdiy_engine* e) {
     CK(cudaMemsetAsync(e->kc, 0, kv * 2, e->stream), "reset K");
     CK(cudaMemsetAsync(e->vc, 0, kv * 2, e->stream), "reset V");
     CK(cudaMemsetAsync(e->x, 0, H * 2, e->stream), "reset x");
-    CK(cudaMemsetAsync(e->q, 0, H * 2, e->stream), "reset q");
-    CK(cudaMemsetAsync(e->att, 0, H * 2, e->stream), "reset att");
-    CK(cudaMemsetAsync(e->act, 0, (size_t)c.intermediate_size * 2, e->stream), "reset act");
     CK(cudaMemsetAsync(e->logits, 0, (size_t)c.vocab_size * 2, e->stream), "reset logits");
     CK(cudaMemsetAsync(e->ctl, 0, sizeof(DecodeControl), e->stream), "reset control");
     CK(cudaStreamSynchronize(e->stream), "reset");
@@ -528,6 +549,35 @@ int llmdiy_engine_decode_async(llmdiy_engine* e, int first_token, int pos, int n
     if (!e) return LLMDIY_ERR_ARG;
     cudaStream_t st = stream ? reinterpret_cast<cudaStream_t>(stream) : e->stream;
     return launch(e, first_token, pos, n_steps, false, stop_on_eos != 0, false, st);
+}
+
+// Timing probes of one decode launch: out[(cta*cap + i)*2] = %globaltimer (ns)
+// at the i-th phase boundary of CTA `cta`; prod[((cta*6 + phase)*8 + warp)*4 +
+// {0,1,2,3}] = SM cycles waiting for ring chunks, computing, issuing copies; chunks.
+int llmdiy_engine_profile(llmdiy_engine* e, int first_token, int pos, int n_steps, int cap, uint64_t* out,
+                          uint64_t* prod) {
+    if (!e || !out || !prod || cap <= 0) return LLMDIY_ERR_ARG;
+    CK(cudaSetDevice(e->device), "cudaSetDevice");
+    unsigned long long *d = nullptr, *dp = nullptr;
+    const size_t n = (size_t)e->num_sms * cap * 2;
+    CK(cudaMalloc(&d, n * 8), "alloc probes");
+    const size_t np = (size_t)e->num_sms * 6 * kConsumerWarps * 4;
+    CK(cudaMalloc(&dp, np * 8), "alloc probes");
+    cudaMemset(d, 0, n * 8);
+    cudaMemset(dp, 0, np * 8);
+    int rc = launch(e, first_token, pos, n_steps, false, false, false, e->stream, d, dp, cap);
+    if (!rc) {
+        cudaError_t c = cudaStreamSynchronize(e->stream);
+        if (c != cudaSuccess) rc = cuda_fail(e, c, "profile");
+    }
+    if (!rc) rc = read_status(e, nullptr);
+    if (!rc) {
+        cudaMemcpy(out, d, n * 8, cudaMemcpyDeviceToHost);
+        cudaMemcpy(prod, dp, np * 8, cudaMemcpyDeviceToHost);
+    }
+    cudaFree(d);
+    cudaFree(dp);
+    return rc;
 }
 
 int llmdiy_engine_status(llmdiy_engine* e, int* n_done) {

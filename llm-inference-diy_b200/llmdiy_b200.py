@@ -96,6 +96,7 @@ def lib() -> ctypes.CDLL:
         "llmdiy_engine_copy_hidden": [P, P],
         "llmdiy_engine_copy_kv": [P, I, I, I, P, P],
         "llmdiy_engine_num_sms": [P],
+        "llmdiy_engine_profile": [P, I, I, I, I, P, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -309,6 +310,17 @@ class Engine:
         self._chk(lib().llmdiy_engine_copy_kv(self._h, layer, pos0, n, k.ctypes.data_as(ctypes.c_void_p),
                                               v.ctypes.data_as(ctypes.c_void_p)), "copy_kv")
         return k.view(np.float16), v.view(np.float16)
+
+    def profile(self, first_token: int, pos: int, n_steps: int, cap: int = 4096):
+        """Timing probes of one decode launch: (barrier ns [cta, cap, 2], producer/consumer stall ns [cta, 2])."""
+        import numpy as np
+        G = self.num_sms
+        out = np.zeros((G, cap, 2), dtype=np.uint64)
+        prod = np.zeros((G, 6, 8, 4), dtype=np.uint64)
+        self._chk(lib().llmdiy_engine_profile(self._h, first_token, pos, n_steps, cap,
+                                              out.ctypes.data_as(ctypes.c_void_p),
+                                              prod.ctypes.data_as(ctypes.c_void_p)), "profile")
+        return out, prod
 
     @property
     def num_sms(self) -> int:
