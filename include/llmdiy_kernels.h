@@ -52,6 +52,16 @@ int llmdiy_fd_v5_split_stage1(const uint16_t* Q, const uint16_t* K, const uint16
  * <<<1,128>>> (qwen_infer.cu:674-676). */
 int llmdiy_fd_opt_stage2(const uint16_t* Opart, const float* LSE, uint16_t* O, int num_chunks, void* stream);
 
+/* No counterpart in the reference.  Split-KV flash decoding of one head in a single launch that
+ * allocates nothing: the same result, bit for bit, as llmdiy_fd_v5_split_stage1 + llmdiy_fd_opt_stage2
+ * with num_chunks = ceil(L/256), but the chunk partials live in a file-scope device array (33,536 bytes)
+ * instead of caller buffers.  L may be at most 32768 rows (128 chunks); a larger L returns -1 before
+ * anything is launched.  The first call on each device looks the array up with cudaGetSymbolAddress and
+ * should come before any stream capture.  Every call on a device shares the array: calls whose work
+ * overlaps on the GPU race; calls ordered on one stream do not. */
+int llmdiy_fd_split_noalloc(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int L, int stride,
+                            void* stream);
+
 /* kernels/argmax.cuh:7 argmax_kernel(out_token, logits, vocab_size), <<<1,512>>> (qwen_infer.cu:731).
  * Reproduces the reference winner among tied maxima; -1 when no value is > -inf. */
 int llmdiy_argmax(int* out, const uint16_t* logits, int V, void* stream);
