@@ -125,12 +125,12 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic():
-    """DRAM bytes per decode token from the committed ncu summary (profiles/), if any."""
+def profile_traffic_ratio():
+    """DRAM bytes (read + write) over algorithmic bytes of decode_kernel, from the committed ncu
+    capture of the small case (profiles/decode_kernel_traffic.json), if present."""
     p = os.path.join(ROOT, "profiles", "decode_kernel_traffic.json")
     if os.path.exists(p):
-        j = json.load(open(p))
-        return j.get("dram_bytes_per_token")
+        return float(json.load(open(p))["traffic_over_algorithmic"])
     return None
 
 
@@ -263,7 +263,7 @@ def run_ours(args, rank, world, local, pg):
     peak, peak_kind = measured_peaks()
     bps = bytes_per_step()
     achieved = bps / (ms / args.steps / 1000.0) / 1e9
-    traffic_tok = profile_traffic()
+    traffic_ratio = profile_traffic_ratio()
 
     # e2e through the public API with host buffers (includes prefill of the 127 prompt tokens)
     for _ in range(max(1, args.warmup // 2)):
@@ -299,7 +299,8 @@ def run_ours(args, rank, world, local, pg):
             "gpu_launches": args.steps,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": (round(traffic_tok * GEN_LEN) if traffic_tok else None),
+                         "traffic": (round(traffic_ratio * bps) if traffic_ratio else None),
+                         "traffic_source": "ncu dram bytes / algorithmic bytes of the 4-layer case, scaled",
                          "algorithmic_bytes_per_launch": bps, "kernel": "decode_kernel (persistent, 256 tokens)"},
             "e2e": {"value": round(e2e_val, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * PROMPT_LEN,
                     "d2h_bytes_per_step": 4 * GEN_LEN},
@@ -311,6 +312,26 @@ def run_ours(args, rank, world, local, pg):
     eng.close()
 
 
+def run_ncu_case():
+    """Small case for ncu captures of decode_kernel: the Qwen-1.8B shapes with 4 layers (full vocab,
+    0.95 GB of weights, larger than L2), one prefill launch of 127 tokens, then one decode launch of
+    2 tokens (capture it with `-k regex:decode_kernel -s 1 -c 1`)."""
+    import torch
+    import llmdiy_b200 as L
+    cfg = L.make_config(**dict(QWEN, num_layers=4), max_seqlen=MAX_SEQLEN)
+    eng = L.Engine(config=cfg, seed=SEED, device=0)
+    prompt = prompt_ids()
+    eng.reset()
+    eng.prefill(prompt[:-1])
+    eng.decode_async(prompt[-1], PROMPT_LEN - 1, 2, stop_on_eos=False)
+    torch.cuda.synchronize()
+    n = eng.status()
+    eng.close()
+    print(json.dumps({"ncu_case": "qwen-1.8b-4layer decode 2 tokens", "n_done": n}), flush=True)
+    if n != 2:
+        sys.exit(1)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -319,7 +340,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-case", action="store_true", help="run the small decode case used for ncu captures")
     args = ap.parse_args()
+    if args.ncu_case:
+        run_ncu_case()
+        return
     rank, world, local, pg = dist_setup(args.gpus)
     try:
         if args.impl == "reference":

@@ -27,6 +27,27 @@ constexpr int kDecodeThreads = kConsumerWarps * 32;
 constexpr int kAttnSplits = 9;       // 16 heads x 9 position splits = 144 attention CTAs
 constexpr int kMaxLayers = 64;       // layer pointers are cached in shared memory
 
+// Units (two weight rows of K elements) in one ring slot: 3 for K = 2048, 1 for K up to 6144.
+__host__ __device__ constexpr int chunk_units(int K) {
+    return kStageBytes / (4 * K) < 1 ? 1 : kStageBytes / (4 * K);
+}
+
+// This CTA's share of one phase's matrix: units [u0, u1), units per chunk, row length K.
+// Phases: 0 qkv (3H/2 units), 1 o_proj (H/2), 2 w12 (IM), 3 c_proj (H/2, K = IM), 4 lm_head (V/2).
+struct PhaseRange {
+    int u0, u1, CH, K;
+};
+__host__ __device__ inline PhaseRange phase_range(int ph, int IM, int V, int b, int G) {
+    const int U = ph == 0 ? 3 * kHidden / 2 : ph == 1 ? kHidden / 2 : ph == 2 ? IM : ph == 3 ? kHidden / 2 : V / 2;
+    const int K = ph == 3 ? IM : kHidden;
+    PhaseRange r;
+    r.u0 = (int)((long long)U * b / G);
+    r.u1 = (int)((long long)U * (b + 1) / G);
+    r.CH = chunk_units(K);
+    r.K = K;
+    return r;
+}
+
 struct LayerPtrs {
     const half* ln1;     // [H]
     const half* qkv_w;   // [3H, H], RoPE-pair permuted rows
@@ -80,7 +101,14 @@ struct DecodeArgs {
     int first_token, pos0, n_steps;
     int skip_lm;              // 1: no lm_head; the input of step t+1 is forced[t+1]
     int stop0, stop1;         // stop ids (-1 = none)
-    int prefetch_owned;       // L2 prefetch distance in owned chunks (0 = off)
+    // Weight-chunk schedule of one step, per CTA: entry i = (byte offset / 16 from wbase, bytes) of
+    // the CTA's i-th chunk (all layers' qkv, o, w12, c chunks, then lm_head's); feed_cnt[2*cta] =
+    // chunks of the layers, feed_cnt[2*cta+1] = chunks of lm_head.  Built once per engine.
+    const uint2* feed_tbl;    // [grid][feed_stride]
+    const int* feed_cnt;      // [grid][2]
+    int feed_stride;
+    const uint8_t* wbase;
+    int l2_ahead;             // L2 prefetch distance in owned chunks beyond the ring (0 = off)
     // optional timing probes (null in production): per CTA and grid barrier,
     // %globaltimer at arrival and at release; per CTA the producer's time
     // blocked on a full ring and the consumers' time waiting for data.

@@ -31,10 +31,6 @@ namespace {
 enum PhaseId { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_W12 = 3, PH_C = 4, PH_LM = 5 };
 
 constexpr int kMaxIM = 6144;
-// Each warp also prefetches into L2 the chunk it will own a.prefetch_owned
-// turns after the one it copies into shared memory (default 2: 16 chunks,
-// ~384 KB per SM, ~57 MB across 148 SMs), so HBM keeps streaming while warps
-// wait for activations.
 constexpr uint32_t kPollLimit = 1u << 21;  // polls of one flag-carrying word or of the step barrier
 
 struct __align__(128) Smem {
@@ -55,10 +51,6 @@ struct __align__(128) Smem {
     int last;
 };
 
-__device__ __forceinline__ int chunk_units(int K) {
-    int u = kStageBytes / (4 * K);
-    return u < 1 ? 1 : u;
-}
 
 // fp32 FMA dot products of two weight rows (a unit) against the activation:
 // K = 2048 with the lane's 64-element activation slice in registers, or any
@@ -134,19 +126,49 @@ __device__ __forceinline__ unsigned long long ll_load(const unsigned long long* 
     asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-// Read N words p[i*stride] that must carry `tag`; data to out[i].  Returns
+// Read N words p[i*stride] that must carry `tag`; data to out[i].  Every
+// poll issues all N loads back to back (a word already received is loaded
+// again and ignored), so one round costs one L2 round trip, not N.  Returns
 // false when the words did not arrive within the poll bound.
 template <int N>
 __device__ __forceinline__ bool ll_read(const unsigned long long* p, int stride, uint32_t tag, uint32_t* out) {
     uint32_t pending = (N == 32) ? 0xffffffffu : ((1u << N) - 1u);
     for (uint32_t it = 0; it < kPollLimit; ++it) {
+        unsigned long long v[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) v[i] = ll_load(p + (size_t)i * stride);
 #pragma unroll
         for (int i = 0; i < N; ++i) {
-            if (pending & (1u << i)) {
-                const unsigned long long v = ll_load(p + (size_t)i * stride);
-                if ((uint32_t)(v >> 32) == tag) {
-                    out[i] = (uint32_t)v;
-                    pending &= ~(1u << i);
+            if ((pending & (1u << i)) && (uint32_t)(v[i] >> 32) == tag) {
+                out[i] = (uint32_t)v[i];
+                pending &= ~(1u << i);
+            }
+        }
+        if (!pending) return true;
+        __nanosleep(it < 8 ? 32 : 128);
+    }
+    return false;
+}
+
+// The SwiGLU output (one fp16 per word, IM <= kMaxIM words): thread tid
+// gathers words tid, tid+256, ... into out[] (shared memory), 12 loads in
+// flight per round.
+__device__ __forceinline__ bool ll_gather_act(const unsigned long long* p, int n, uint32_t tag, half* out) {
+    static_assert(kMaxIM <= 24 * kDecodeThreads, "two rounds of 12 words per thread");
+    uint32_t pending = (1u << n) - 1u;  // n <= 24
+    for (uint32_t it = 0; it < kPollLimit; ++it) {
+#pragma unroll
+        for (int j0 = 0; j0 < 24; j0 += 12) {
+            if (!(pending >> j0)) continue;
+            unsigned long long v[12];
+#pragma unroll
+            for (int j = 0; j < 12; ++j) v[j] = (j0 + j < n) ? ll_load(p + (size_t)(j0 + j) * kDecodeThreads) : 0ull;
+#pragma unroll
+            for (int j = 0; j < 12; ++j) {
+                const int k = j0 + j;
+                if ((pending & (1u << k)) && (uint32_t)(v[j] >> 32) == tag) {
+                    out[(size_t)k * kDecodeThreads] = __ushort_as_half((uint16_t)v[j]);
+                    pending &= ~(1u << k);
                 }
             }
         }
@@ -156,11 +178,17 @@ __device__ __forceinline__ bool ll_read(const unsigned long long* p, int stride,
     return false;
 }
 
-// Timing probe (development aid, off when a.prof is null): thread 0 of each
-// CTA stamps %globaltimer at consecutive indices of its row of a.prof.
+// Timing probe (development aid, off when a.prof is null): at consecutive
+// boundaries of its row of a.prof, each CTA records %globaltimer when warp 0
+// arrives (slot 0) and when the last of its warps arrives (slot 1).
 __device__ __forceinline__ void probe(const DecodeArgs& a, int tid, int& np) {
-    if (a.prof && tid == 0) {
-        if (np < a.prof_cap) a.prof[((size_t)blockIdx.x * a.prof_cap + np) * 2] = globaltimer();
+    if (a.prof) {
+        if ((tid & 31) == 0 && np < a.prof_cap) {
+            const unsigned long long t = globaltimer();
+            unsigned long long* p = a.prof + ((size_t)blockIdx.x * a.prof_cap + np) * 2;
+            if (tid == 0) p[0] = t;
+            atomicMax(p + 1, t);
+        }
         ++np;
     }
 }
@@ -177,77 +205,60 @@ struct Tags {
 // Walks this CTA's chunk sequence: per step, per layer the chunks of qkv_w,
 // proj_w, w12, cproj, then (unless skip_lm) lm_head.  Chunk i of the
 // sequence goes to ring slot i % 8.
-struct Feed {
-    int step, layer, phase;  // phase 0..3 = qkv, o, w12, c; 4 = lm_head
-    int cu, u1, CH, K;       // current unit, end of this CTA's range, units per chunk, row length
-    const half* W;
-    uint32_t chunk;          // sequence index of the current position
+// Producer side of a warp's ring slot: a cursor over the CTA's chunk schedule
+// (DecodeArgs::feed_tbl), visiting the chunks this warp owns (index = warp
+// mod 8) in order across layers, phases and steps.  The table entry of the
+// next chunk is loaded one issue ahead, so issuing costs two instructions.
+// A second cursor, a.l2_ahead owned chunks further on, prefetches into L2
+// so that HBM keeps streaming while the ring is full.
+struct Cursor {
+    int i, step;    // index in the step's schedule, step
+    uint2 ent;      // its table entry
     bool done;
 };
+struct Feed {
+    int E;          // chunks per step of this CTA
+    uint32_t g;     // global index of cur (step * E + i): the ring phase parity is (g >> 3) & 1
+    uint32_t last;  // global index of the last chunk issued (0xffffffff: none)
+    Cursor cur, pre;
+};
 
-__device__ __forceinline__ void feed_enter_phase(const DecodeArgs& a, const Smem& s, Feed& f) {
-    // move to the first non-empty phase at or after (step, layer, phase)
-    for (;;) {
-        if (f.step >= a.n_steps) { f.done = true; return; }
-        const half* W;
-        if (f.phase == 4) {
-            W = a.lm_head;
-        } else {
-            const LayerPtrs& L = s.layers[f.layer];
-            W = f.phase == 0 ? L.qkv_w : f.phase == 1 ? L.proj_w : f.phase == 2 ? L.w12 : L.cproj;
-        }
-        const int K = s.range[f.phase][3];
-        f.cu = s.range[f.phase][0];
-        f.u1 = s.range[f.phase][1];
-        f.CH = s.range[f.phase][2];
-        f.K = K;
-        f.W = W;
-        if (f.cu < f.u1) return;
-        // empty range: next phase
-        if (f.phase == 4 || (f.phase == 3 && f.layer == a.NL - 1)) {
-            if (f.phase == 3 && !a.skip_lm) { f.phase = 4; continue; }
-            f.step++; f.layer = 0; f.phase = 0;
-        } else if (f.phase == 3) {
-            f.layer++; f.phase = 0;
-        } else {
-            f.phase++;
-        }
-    }
+__device__ __forceinline__ void cursor_step(const DecodeArgs& a, Cursor& c, int E, int by) {
+    c.i += by;
+    while (c.i >= E) { c.i -= E; c.step++; }
+    c.done = c.step >= a.n_steps;
+    if (!c.done) c.ent = __ldg(a.feed_tbl + (size_t)blockIdx.x * a.feed_stride + c.i);
 }
 
-__device__ __forceinline__ void feed_advance(const DecodeArgs& a, const Smem& s, Feed& f) {
-    f.cu += f.CH;
-    f.chunk++;
-    if (f.cu < f.u1) return;
-    if (f.phase == 4 || (f.phase == 3 && f.layer == a.NL - 1)) {
-        if (f.phase == 3 && !a.skip_lm) f.phase = 4;
-        else { f.step++; f.layer = 0; f.phase = 0; }
-    } else if (f.phase == 3) {
-        f.layer++; f.phase = 0;
-    } else {
-        f.phase++;
-    }
-    feed_enter_phase(a, s, f);
+__device__ __forceinline__ void feed_init(const DecodeArgs& a, Feed& f, int warp) {
+    const int b = blockIdx.x;
+    f.E = a.feed_cnt[2 * b] + (a.skip_lm ? 0 : a.feed_cnt[2 * b + 1]);
+    f.g = (uint32_t)warp;
+    f.last = 0xffffffffu;
+    f.cur.i = 0;
+    f.cur.step = 0;
+    f.cur.done = true;
+    f.pre = f.cur;
+    if (f.E <= 0) return;
+    cursor_step(a, f.cur, f.E, warp);
+    f.pre = f.cur;
+    if (a.l2_ahead > 0) cursor_step(a, f.pre, f.E, kRingStages * a.l2_ahead);
+    else f.pre.done = true;
 }
 
 // Issue the copy of the next chunk owned by `warp` (lane 0 only).
 __device__ __forceinline__ void feed_issue_next(const DecodeArgs& a, Feed& f, Smem& s, int warp, uint64_t pol) {
-    while (!f.done && (int)(f.chunk & (kRingStages - 1)) != warp) feed_advance(a, s, f);
-    if (f.done) return;
-    const int nun = (f.u1 - f.cu) < f.CH ? (f.u1 - f.cu) : f.CH;
-    const uint32_t bytes = (uint32_t)nun * 4u * (uint32_t)f.K;
+    if (f.cur.done) return;
+    const uint32_t bytes = f.cur.ent.y;
     mbar_arrive_expect_tx(&s.full[warp], bytes);
-    bulk_g2s(s.ring[warp], f.W + (size_t)f.cu * 2 * f.K, bytes, &s.full[warp], pol);
-    feed_advance(a, s, f);
-}
-
-// L2 prefetch of the next chunk owned by `warp` on a second cursor.
-__device__ __forceinline__ void feed_prefetch_next(const DecodeArgs& a, const Smem& s, Feed& f, int warp) {
-    while (!f.done && (int)(f.chunk & (kRingStages - 1)) != warp) feed_advance(a, s, f);
-    if (f.done) return;
-    const int nun = (f.u1 - f.cu) < f.CH ? (f.u1 - f.cu) : f.CH;
-    bulk_prefetch_l2(f.W + (size_t)f.cu * 2 * f.K, (uint32_t)nun * 4u * (uint32_t)f.K);
-    feed_advance(a, s, f);
+    bulk_g2s(s.ring[warp], a.wbase + (size_t)f.cur.ent.x * 16u, bytes, &s.full[warp], pol);
+    f.last = f.g;
+    f.g += kRingStages;
+    cursor_step(a, f.cur, f.E, kRingStages);
+    if (!f.pre.done) {
+        bulk_prefetch_l2(a.wbase + (size_t)f.pre.ent.x * 16u, f.pre.ent.y);
+        cursor_step(a, f.pre, f.E, kRingStages);
+    }
 }
 
 // ------------------------------------------------------------------ consumers
@@ -293,8 +304,9 @@ __device__ bool grid_sync(const DecodeArgs& a, Smem& s, uint32_t& nbar, int tid,
 // of the normalised vector in xr.  The source is either a plain fp16 row (the
 // embedding) or flag-carrying words with `tag`.  Returns the CTA-wide failure
 // verdict (true = a wait expired somewhere in the CTA).
-__device__ bool load_norm(const half* plain, const unsigned long long* ll, uint32_t tag, const half* w, Smem& s,
-                          int tid, float* xr, bool bad) {
+__device__ bool load_norm(const DecodeArgs& a, const half* plain, const unsigned long long* ll, uint32_t tag,
+                          const half* w, Smem& s, int tid, float* xr, bool bad, int& np) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + tid * 8);  // in flight while polling
     uint4 v;
     if (plain) {
         v = *reinterpret_cast<const uint4*>(plain + tid * 8);
@@ -305,11 +317,12 @@ __device__ bool load_norm(const half* plain, const unsigned long long* ll, uint3
     }
     // the previous phase may still read xraw / xs: wait before overwriting
     if (named_bar_or(1, 256, bad)) return true;
+    probe(a, tid, np);
     *reinterpret_cast<uint4*>(s.xraw + tid * 8) = v;
     const float r = rms_scale_tree256(s.xraw, kHidden, 1e-6f, s.red, tid, 1);
     float xf[8], wf[8], of[8];
     unpack8(v, xf);
-    unpack8(*reinterpret_cast<const uint4*>(w + tid * 8), wf);
+    unpack8(wv, wf);
 #pragma unroll
     for (int e = 0; e < 8; ++e) of[e] = (xf[e] * r) * wf[e];
     *reinterpret_cast<uint4*>(s.xs + tid * 8) = pack8(of);
@@ -320,10 +333,9 @@ __device__ bool load_norm(const half* plain, const unsigned long long* ll, uint3
     return false;
 }
 
-template <int PH>
-__device__ __forceinline__ void epilogue(const DecodeArgs& a, const Smem& s, StepCtx& c, int u, float s0, float s1,
-                                         float bias0, float bias1) {
-    if constexpr (PH == PH_QKV) {
+__device__ __forceinline__ void epilogue(int ph, const DecodeArgs& a, const Smem& s, StepCtx& c, int u, float s0,
+                                         float s1, float bias0, float bias1) {
+    if (ph == PH_QKV) {
         const int sec = u / (kHidden / 2), v = u % (kHidden / 2), h = v / 64, t = v % 64;
         const float y1 = h2f(f2h(h2f(f2h(s0)) + bias0));
         const float y2 = h2f(f2h(h2f(f2h(s1)) + bias1));
@@ -347,21 +359,21 @@ __device__ __forceinline__ void epilogue(const DecodeArgs& a, const Smem& s, Ste
             }
         }
         ll_store(a.ll_qkv + u, (uint32_t)__half_as_ushort(r1) | ((uint32_t)__half_as_ushort(r2) << 16), c.tag);
-    } else if constexpr (PH == PH_O || PH == PH_C) {
+    } else if (ph == PH_O || ph == PH_C) {
         const int n = 2 * u;
         const half2 xo = *reinterpret_cast<const half2*>(s.xraw + n);
         const half2 r = __floats2half2_rn(h2f(__low2half(xo)) + h2f(f2h(s0)), h2f(__high2half(xo)) + h2f(f2h(s1)));
         const uint32_t bits = *reinterpret_cast<const uint32_t*>(&r);
-        if constexpr (PH == PH_O) {
+        if (ph == PH_O) {
             ll_store(a.ll_xo + u, bits, c.tag);
         } else {
             ll_store(a.ll_xc + u, bits, c.tag);
             if (c.layer == a.NL - 1) *reinterpret_cast<half2*>(a.x + n) = r;
         }
-    } else if constexpr (PH == PH_W12) {
+    } else if (ph == PH_W12) {
         const float g = h2f(f2h(s0)), up = h2f(f2h(s1));
         ll_store(a.ll_act + u, (uint32_t)__half_as_ushort(f2h(g * __fdividef(up, 1.0f + __expf(-up)))), c.tag);
-    } else if constexpr (PH == PH_LM) {
+    } else {  // PH_LM
         const int n = 2 * u;
         const half l0 = f2h(s0), l1 = f2h(s1);
         *reinterpret_cast<half2*>(a.logits + n) = __halves2half2(l0, l1);
@@ -374,12 +386,15 @@ __device__ __forceinline__ void epilogue(const DecodeArgs& a, const Smem& s, Ste
 
 // Consume this CTA's chunks of one weight matrix (rows in units of two).
 // A wait that expires marks `bad` and the remaining chunks are skipped.
-template <int PH, bool kRegs>
-__device__ void gemv_phase(const DecodeArgs& a, Smem& s, StepCtx& c, int K, uint32_t& chunk, const float* xr,
-                           int warp, int lane, bool& bad, Feed& feed, Feed& pre, uint64_t pol) {
-    constexpr int R = PH == PH_QKV ? 0 : PH == PH_O ? 1 : PH == PH_W12 ? 2 : PH == PH_C ? 3 : 4;
-    const int u0 = s.range[R][0], u1 = s.range[R][1], CH = s.range[R][2];
+// Phases run through one call site so the kernel's code stays small enough
+// for the instruction caches (the phase id selects range, dot and epilogue).
+__device__ __forceinline__ void gemv_phase(int PH, const DecodeArgs& a, Smem& s, StepCtx& c, uint32_t& chunk,
+                                           const float* xr, int warp, int lane, bool& bad, Feed& feed,
+                                           uint64_t pol) {
+    const int R = PH == PH_LM ? 4 : PH == PH_C ? 3 : PH == PH_W12 ? 2 : PH == PH_O ? 1 : 0;
+    const int u0 = s.range[R][0], u1 = s.range[R][1], CH = s.range[R][2], K = s.range[R][3];
     unsigned long long pw = 0, pc = 0, pi = 0, pn = 0;  // probe sums (profiling only)
+    unsigned long long pmaxw = 0;  // DEBUG: longest single wait
     for (int cu = u0; cu < u1; cu += CH, ++chunk) {
         if ((int)(chunk & (kRingStages - 1)) != warp) continue;
         const int nun = (u1 - cu) < CH ? (u1 - cu) : CH;
@@ -394,7 +409,7 @@ __device__ void gemv_phase(const DecodeArgs& a, Smem& s, StepCtx& c, int K, uint
         const unsigned long long t1 = a.prof_prod ? (unsigned long long)clock64() : 0ull;
         // QKV: the bias pair of unit `lane` is fetched before the dot products
         float b0 = 0.f, b1 = 0.f;
-        if constexpr (PH == PH_QKV) {
+        if (PH == PH_QKV) {
             if (lane < nun) {
                 const int u = cu + lane, sec = u / (kHidden / 2), v = u % (kHidden / 2);
                 const int i1 = sec * kHidden + (v / 64) * kHeadDim + (v % 64);
@@ -404,39 +419,62 @@ __device__ void gemv_phase(const DecodeArgs& a, Smem& s, StepCtx& c, int K, uint
         }
         const half* buf = reinterpret_cast<const half*>(s.ring[warp]);
         float r0s = 0.f, r1s = 0.f;  // lane j keeps unit j's two dot products
-#pragma unroll
-        for (int j = 0; j < 3; ++j) {
-            if (j < nun) {
-                const half* r0 = buf + (size_t)j * 2 * K;
-                float s0, s1;
-                if constexpr (kRegs) dot2_regs(r0, r0 + K, xr, lane, s0, s1);
-                else dot2_smem(r0, r0 + K, s.act, K, lane, s0, s1);
-                if (lane == j) { r0s = s0; r1s = s1; }
-            }
+#pragma unroll 1
+        for (int j = 0; j < nun; ++j) {
+            const half* r0 = buf + (size_t)j * 2 * K;
+            float s0, s1;
+            if (PH == PH_C) dot2_smem(r0, r0 + K, s.act, K, lane, s0, s1);
+            else dot2_regs(r0, r0 + K, xr, lane, s0, s1);
+            if (lane == j) { r0s = s0; r1s = s1; }
         }
-        if (lane < nun) epilogue<PH>(a, s, c, cu + lane, r0s, r1s, b0, b1);
+        if (lane < nun) epilogue(PH, a, s, c, cu + lane, r0s, r1s, b0, b1);
         __syncwarp();
         const unsigned long long t2 = a.prof_prod ? (unsigned long long)clock64() : 0ull;
-        // the slot is drained: stream this warp's next chunk into it, and
-        // prefetch into L2 the one a.prefetch_owned turns further on
-        if (lane == 0) {
-            feed_issue_next(a, feed, s, warp, pol);
-            if (a.prefetch_owned > 0) feed_prefetch_next(a, s, pre, warp);
-        }
+        // the slot is drained: stream this warp's next chunk into it
+        if (lane == 0) feed_issue_next(a, feed, s, warp, pol);
         if (a.prof_prod) {
             pw += t1 - t0;
+            pmaxw = (t1 - t0) > pmaxw ? (t1 - t0) : pmaxw;
             pc += t2 - t1;
             pi += (unsigned long long)clock64() - t2;
             pn += 1;
         }
     }
-    if (a.prof_prod && lane == 0 && pn) {
+    if (a.prof_prod && lane == 0) {
         // per CTA, phase and warp: SM cycles waiting for chunks, computing, issuing; chunks
         unsigned long long* q = a.prof_prod + (((size_t)blockIdx.x * 6 + PH) * kConsumerWarps + warp) * 4;
-        q[0] += pw;
-        q[1] += pc;
-        q[2] += pi;
-        q[3] += pn;
+        atomicAdd(q, pw);  // reductions: no round trip on the phase's critical path
+        atomicAdd(q + 1, pc);
+        atomicAdd(q + 2, pi);
+        atomicMax(q + 3, pmaxw);  // DEBUG: longest single wait
+    }
+}
+
+__device__ __forceinline__ void prefetch_l2_line(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// L2 prefetch, one line per thread, of what the critical path of the coming
+// phases reads from global memory besides flag words: the next layer's ln_1,
+// ln_2 and QKV bias (ln_f as well at the last layer), and this CTA's rows of
+// the KV cache for the attention phase (rows before pos, written by earlier
+// steps).  With HBM saturated by the weight stream, a demand miss on these
+// would cost several microseconds on the critical path.
+__device__ void prefetch_critical(const DecodeArgs& a, const Smem& s, const StepCtx& c, int l, int tid) {
+    const LayerPtrs& N = s.layers[l + 1 < a.NL ? l + 1 : 0];
+    if (tid < 32) prefetch_l2_line(N.ln1 + tid * 64);
+    else if (tid < 64) prefetch_l2_line(N.ln2 + (tid - 32) * 64);
+    else if (tid < 160) prefetch_l2_line(N.qkv_b + (tid - 64) * 64);
+    else if (tid < 192 && l + 1 == a.NL) prefetch_l2_line(a.lnf + (tid - 160) * 64);
+    const int b = blockIdx.x;
+    if (b < kHeads * kAttnSplits) {
+        const int h = b / kAttnSplits, sp = b % kAttnSplits, L = c.pos + 1;
+        const int r0 = (int)((long long)L * sp / kAttnSplits), r1 = (int)((long long)L * (sp + 1) / kAttnSplits);
+        const int rend = (r1 == L) ? L - 1 : r1;
+        for (int i = tid; i < (rend - r0) * 4; i += kDecodeThreads) {
+            const half* base = ((i & 2) ? c.vcl : c.kcl) + (size_t)(r0 + (i >> 2)) * kHidden + h * kHeadDim;
+            prefetch_l2_line(base + (i & 1) * 64);
+        }
     }
 }
 
@@ -556,44 +594,40 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
     c.ipt = (a.V + 511) / 512;
     const Tags tags{a.flag_base, a.NL};
     bool bad = false;
-    int np = 0;  // probe index (thread 0)
+    int np = 0;  // probe index
     const uint64_t pol = l2_policy_evict_first();
     Feed feed{};
-    feed.step = 0; feed.layer = 0; feed.phase = 0; feed.chunk = 0; feed.done = false;
-    Feed pre = feed;
     if (lane == 0) {
-        feed_enter_phase(a, s, feed);
+        feed_init(a, feed, warp);
         feed_issue_next(a, feed, s, warp, pol);  // this warp's first chunk
-        pre = feed;                              // L2 prefetch cursor starts at the next owned chunk
-        for (int i = 0; i < a.prefetch_owned; ++i) feed_prefetch_next(a, s, pre, warp);
     }
     for (int step = 0; step < a.n_steps; ++step) {
         c.pos = a.pos0 + step;
         c.step = step;
-        const half* emb = a.wte + (size_t)token * kHidden;
         bool failed = false;
-        for (int l = 0; l < a.NL; ++l) {
+        // Phases of the step: per layer QKV, O, W12, C (qwen_infer.cu:626-721), then LM
+        // (qwen_infer.cu:725-731).  Each phase: probe A, prologue (its input vector
+        // into xr or s.act; probe B once the input words have arrived), probe C, GEMV.
+        const int nph = a.NL * 4 + (a.skip_lm ? 0 : 1);
+#pragma unroll 1
+        for (int k = 0; k < nph; ++k) {
+            const int ph = k == a.NL * 4 ? PH_LM : (k & 3) == 0 ? PH_QKV : (k & 3) == 1 ? PH_O : (k & 3) == 2 ? PH_W12 : PH_C;
+            const int l = ph == PH_LM ? a.NL - 1 : k >> 2;
             const LayerPtrs& L = s.layers[l];
-            c.layer = l;
-            c.kcl = a.kc + (size_t)l * a.max_seqlen * kHidden;
-            c.vcl = a.vc + (size_t)l * a.max_seqlen * kHidden;
-            c.bias = L.qkv_b;
-            // QKV (qwen_infer.cu:626-642)
+            if (ph == PH_QKV) {
+                c.layer = l;
+                c.kcl = a.kc + (size_t)l * a.max_seqlen * kHidden;
+                c.vcl = a.vc + (size_t)l * a.max_seqlen * kHidden;
+                c.bias = L.qkv_b;
+                prefetch_critical(a, s, c, l, tid);
+            }
             probe(a, tid, np);
-            failed = (l == 0) ? load_norm(emb, nullptr, 0, L.ln1, s, tid, xr, bad)
-                              : load_norm(nullptr, a.ll_xc, tags(step, l - 1, LL_XC), L.ln1, s, tid, xr, bad);
-            if (failed) break;
-            c.tag = tags(step, l, LL_QKV);
-            probe(a, tid, np);
-            gemv_phase<PH_QKV, true>(a, s, c, kHidden, chunk, xr, warp, lane, bad, feed, pre, pol);
-            // attention (qwen_infer.cu:646-677)
-            probe(a, tid, np);
-            failed = attention_phase(a, s, c, tags, tid, bad);
-            if (failed) break;
-            probe(a, tid, np);
-            // o_proj + residual (qwen_infer.cu:701-704): each thread polls its own
-            // four words of att into shared memory, then every warp takes its slice
-            {
+            if (ph == PH_O) {
+                // attention (qwen_infer.cu:646-677), then each thread polls its own
+                // four words of att into shared memory and every warp takes its slice
+                failed = attention_phase(a, s, c, tags, tid, bad);
+                if (failed) break;
+                probe(a, tid, np);
                 uint32_t d[4];
                 bad |= !ll_read<4>(a.ll_att + 4 * tid, 1, tags(step, l, LL_ATT), d);
                 failed = named_bar_or(1, 256, bad);  // the previous phase is done with s.xs
@@ -603,34 +637,31 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
                     unpack8(*reinterpret_cast<const uint4*>(s.xs + 256 * j + 8 * lane), xr + 8 * j);
-            }
-            c.tag = tags(step, l, LL_XO);
-            probe(a, tid, np);
-            gemv_phase<PH_O, true>(a, s, c, kHidden, chunk, xr, warp, lane, bad, feed, pre, pol);
-            // RMSNorm + w1/w2 + SwiGLU (qwen_infer.cu:708-715)
-            probe(a, tid, np);
-            failed = load_norm(nullptr, a.ll_xo, tags(step, l, LL_XO), L.ln2, s, tid, xr, bad);
-            if (failed) break;
-            c.tag = tags(step, l, LL_ACT);
-            probe(a, tid, np);
-            gemv_phase<PH_W12, true>(a, s, c, kHidden, chunk, xr, warp, lane, bad, feed, pre, pol);
-            probe(a, tid, np);
-            // c_proj + residual (qwen_infer.cu:718-721).  s.act was last read by the
-            // previous layer's C phase, which every warp has left (several named
-            // barriers since), so the words go straight to shared memory.
-            {
-                const uint32_t ta = tags(step, l, LL_ACT);
-                for (int i = tid; i < a.IM; i += 256) {
-                    uint32_t d[1] = {0};
-                    bad |= !ll_read<1>(a.ll_act + i, 1, ta, d);
-                    s.act[i] = __ushort_as_half((uint16_t)d[0]);
-                }
+            } else if (ph == PH_C) {
+                // SwiGLU output into s.act.  s.act was last read by the previous
+                // layer's C phase, which every warp has left (several named
+                // barriers since), so the words go straight to shared memory.
+                const int n = (a.IM - tid + kDecodeThreads - 1) / kDecodeThreads;
+                bad |= !ll_gather_act(a.ll_act + tid, n, tags(step, l, LL_ACT), s.act + tid);
                 failed = named_bar_or(1, 256, bad);
                 if (failed) break;
+                probe(a, tid, np);
+            } else {
+                // RMSNorm of the residual stream: the embedding row (first layer),
+                // the previous layer's output, or this layer's attention residual
+                const half* plain = (ph == PH_QKV && l == 0) ? a.wte + (size_t)token * kHidden : nullptr;
+                const unsigned long long* src = ph == PH_W12 ? a.ll_xo : a.ll_xc;
+                const uint32_t tag = ph == PH_W12 ? tags(step, l, LL_XO)
+                                     : ph == PH_LM ? tags(step, l, LL_XC)
+                                                   : (l > 0 ? tags(step, l - 1, LL_XC) : 0u);
+                const half* w = ph == PH_QKV ? L.ln1 : ph == PH_W12 ? L.ln2 : a.lnf;
+                failed = load_norm(a, plain, src, tag, w, s, tid, xr, bad, np);
+                if (failed) break;
             }
-            c.tag = tags(step, l, LL_XC);
+            c.tag = tags(step, l, ph == PH_QKV ? LL_QKV : ph == PH_O ? LL_XO : ph == PH_W12 ? LL_ACT : LL_XC);
+            c.best = 0ull;
             probe(a, tid, np);
-            gemv_phase<PH_C, false>(a, s, c, a.IM, chunk, xr, warp, lane, bad, feed, pre, pol);
+            gemv_phase(ph, a, s, c, chunk, xr, warp, lane, bad, feed, pol);
         }
         if (failed) break;
         if (a.skip_lm) {
@@ -640,12 +671,7 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
             if (blockIdx.x == 0 && tid == 0) a.ctl->n_done = step + 1;
             continue;
         }
-        // final RMSNorm + lm_head + argmax (qwen_infer.cu:725-731)
-        probe(a, tid, np);
-        if (load_norm(nullptr, a.ll_xc, tags(step, a.NL - 1, LL_XC), a.lnf, s, tid, xr, bad)) break;
-        c.best = 0ull;
-        probe(a, tid, np);
-        gemv_phase<PH_LM, true>(a, s, c, kHidden, chunk, xr, warp, lane, bad, feed, pre, pol);
+        // argmax over the CTAs' best keys (argmax.cuh tie rule, see argmax_key)
         c.best = warp_max_u64(c.best);  // lanes 0..2 each tracked their own units
         if (lane == 0) s.wkey[warp] = c.best;
         named_bar_sync(1, 256);
@@ -682,14 +708,7 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
     // Drain: the last copy this warp issued must have landed before the CTA
     // exits (waiting on an already-consumed chunk returns at once: no later
     // copy went to this slot).
-    if (lane == 0 && feed.chunk > 0) {
-        uint32_t last = feed.chunk - 1;
-        const uint32_t r = (uint32_t)warp;
-        if ((last & 7u) >= r) last -= (last & 7u) - r;
-        else if (last >= 8u) last = last - (last & 7u) - 8u + r;
-        else last = 0xffffffffu;
-        if (last != 0xffffffffu) mbar_wait(&s.full[warp], (last >> 3) & 1);
-    }
+    if (lane == 0 && feed.last != 0xffffffffu) mbar_wait(&s.full[warp], (feed.last >> 3) & 1);
 }
 
 __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeArgs a) {
@@ -704,14 +723,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         reinterpret_cast<uint64_t*>(s.layers)[i] = reinterpret_cast<const uint64_t*>(a.layers)[i];
     if (threadIdx.x < 5) {
         // this CTA's unit range of each phase: the same for every layer and step
-        const int ph = threadIdx.x;
-        const int U = ph == 0 ? 3 * kHidden / 2 : ph == 1 ? kHidden / 2 : ph == 2 ? a.IM : ph == 3 ? kHidden / 2 : a.V / 2;
-        const int K = ph == 3 ? a.IM : kHidden;
-        const int b = blockIdx.x, G = gridDim.x;
-        s.range[ph][0] = (int)((long long)U * b / G);
-        s.range[ph][1] = (int)((long long)U * (b + 1) / G);
-        s.range[ph][2] = chunk_units(K);
-        s.range[ph][3] = K;
+        const PhaseRange r = phase_range(threadIdx.x, a.IM, a.V, blockIdx.x, gridDim.x);
+        s.range[threadIdx.x][0] = r.u0;
+        s.range[threadIdx.x][1] = r.u1;
+        s.range[threadIdx.x][2] = r.CH;
+        s.range[threadIdx.x][3] = r.K;
     }
     __syncthreads();
     consumers(a, s);

@@ -82,7 +82,10 @@ struct llmdiy_engine {
     unsigned long long* ll = nullptr;  // flag-carrying words: qkv | att | xo | act | xc
     size_t ll_words = 0;
     uint32_t tag_base = 0;
-    int prefetch_owned = 0;  // L2 prefetch distance of the decode kernel (LLMDIY_L2_PREFETCH overrides)
+    uint2* feed_tbl = nullptr;  // decode kernel's per-CTA weight-chunk schedule of one step
+    int* feed_cnt = nullptr;
+    int feed_stride = 0;
+    int l2_ahead = 0;  // decode kernel's L2 prefetch distance (env LLMDIY_L2_AHEAD)
     DecodeControl* ctl = nullptr;
     int* tokens_dev = nullptr;
     int* forced_dev = nullptr;
@@ -258,6 +261,45 @@ int alloc_state(llmdiy_engine* e) {
     return llmdiy_engine_reset(e);
 }
 
+// The decode kernel's weight-chunk schedule: for every CTA, the chunks it
+// streams in one step, in consumption order (per layer qkv, o_proj, w12,
+// c_proj; then lm_head), as (offset / 16 from the weight buffer, bytes).
+int build_feed_table(llmdiy_engine* e) {
+    const llmdiy_config& c = e->cfg;
+    const int G = e->num_sms, NL = (int)c.num_layers, IM = (int)c.intermediate_size, V = (int)c.vocab_size;
+    std::vector<std::vector<uint2>> per(G);
+    std::vector<int> cnt(2 * G);
+    auto add = [&](std::vector<uint2>& v, const half* W, const PhaseRange& r) {
+        for (int cu = r.u0; cu < r.u1; cu += r.CH) {
+            const int nun = std::min(r.CH, r.u1 - cu);
+            const size_t off = (size_t)(reinterpret_cast<const uint8_t*>(W + (size_t)cu * 2 * r.K) - e->wbuf);
+            v.push_back(make_uint2((uint32_t)(off / 16), (uint32_t)nun * 4u * (uint32_t)r.K));
+        }
+    };
+    for (int b = 0; b < G; ++b) {
+        PhaseRange r[5];
+        for (int ph = 0; ph < 5; ++ph) r[ph] = phase_range(ph, IM, V, b, G);
+        for (int l = 0; l < NL; ++l) {
+            const LayerPtrs& L = e->layers[l];
+            add(per[b], L.qkv_w, r[0]);
+            add(per[b], L.proj_w, r[1]);
+            add(per[b], L.w12, r[2]);
+            add(per[b], L.cproj, r[3]);
+        }
+        cnt[2 * b] = (int)per[b].size();
+        add(per[b], e->lm_head, r[4]);
+        cnt[2 * b + 1] = (int)per[b].size() - cnt[2 * b];
+        e->feed_stride = std::max(e->feed_stride, (int)per[b].size());
+    }
+    std::vector<uint2> flat((size_t)G * e->feed_stride, make_uint2(0, 0));
+    for (int b = 0; b < G; ++b) std::copy(per[b].begin(), per[b].end(), flat.begin() + (size_t)b * e->feed_stride);
+    CK(cudaMalloc(&e->feed_tbl, flat.size() * sizeof(uint2)), "alloc chunk schedule");
+    CK(cudaMalloc(&e->feed_cnt, cnt.size() * sizeof(int)), "alloc chunk counts");
+    CK(cudaMemcpy(e->feed_tbl, flat.data(), flat.size() * sizeof(uint2), cudaMemcpyHostToDevice), "upload schedule");
+    CK(cudaMemcpy(e->feed_cnt, cnt.data(), cnt.size() * sizeof(int), cudaMemcpyHostToDevice), "upload counts");
+    return LLMDIY_OK;
+}
+
 int create_common(llmdiy_engine* e, Source& src) {
     CK(cudaSetDevice(e->device), "cudaSetDevice");
     cudaDeviceProp prop;
@@ -268,8 +310,9 @@ int create_common(llmdiy_engine* e, Source& src) {
     if (prop.sharedMemPerBlockOptin < decode_smem_bytes())
         return fail(e, LLMDIY_ERR_UNSUPPORTED, "not enough shared memory per block for the decode kernel");
     CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "cudaStreamCreate");
-    if (const char* pf = std::getenv("LLMDIY_L2_PREFETCH")) e->prefetch_owned = std::max(0, std::atoi(pf));
+    if (const char* v = std::getenv("LLMDIY_L2_AHEAD")) e->l2_ahead = std::max(0, std::atoi(v));
     int rc = load_weights(e, src);
+    if (!rc) rc = build_feed_table(e);
     if (rc) return rc;
     return alloc_state(e);
 }
@@ -325,7 +368,11 @@ int launch(llmdiy_engine* e, int first_token, int pos0, int n_steps, bool skip_l
     a.skip_lm = skip_lm ? 1 : 0;
     a.stop0 = stop_on_eos ? 151645 : -1;  // qwen_infer.cu:808
     a.stop1 = stop_on_eos ? 151643 : -1;
-    a.prefetch_owned = e->prefetch_owned;
+    a.feed_tbl = e->feed_tbl;
+    a.feed_cnt = e->feed_cnt;
+    a.feed_stride = e->feed_stride;
+    a.wbase = e->wbuf;
+    a.l2_ahead = e->l2_ahead;
     a.prof = prof;
     a.prof_prod = prof_prod;
     a.prof_cap = prof_cap;
@@ -418,6 +465,8 @@ void llmdiy_engine_destroy(llmdiy_engine* e) {
     cudaSetDevice(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
     cudaFree(e->wbuf);
+    cudaFree(e->feed_tbl);
+    cudaFree(e->feed_cnt);
     cudaFree(e->d_layers);
     cudaFree(e->kc);
     cudaFree(e->vc);
