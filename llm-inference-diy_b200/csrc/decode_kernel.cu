@@ -52,27 +52,37 @@ struct __align__(128) Smem {
 };
 
 
-// fp32 FMA dot products of two weight rows (a unit) against the activation:
-// K = 2048 with the lane's 64-element activation slice in registers, or any
-// K with the activation in shared memory.  After the butterfly every lane
-// holds both sums.
-__device__ __forceinline__ void dot2_regs(const half* r0, const half* r1, const float* xr, int lane, float& s0,
+// acc0 += lo(w) * lo(x), acc1 += hi(w) * hi(x): fp16 operands, exact product,
+// fp32 accumulate (the same arithmetic as fmaf(float(w), float(x), acc)).
+__device__ __forceinline__ void fma2_f16(float& acc0, float& acc1, uint32_t w, uint32_t x) {
+    asm("{\n\t.reg .f16 wl, wh, xl, xh;\n\t"
+        "mov.b32 {wl, wh}, %2;\n\t"
+        "mov.b32 {xl, xh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, wl, xl, %0;\n\t"
+        "fma.rn.f32.f16 %1, wh, xh, %1;\n\t}"
+        : "+f"(acc0), "+f"(acc1)
+        : "r"(w), "r"(x));
+}
+
+// fp32-accumulated dot products of two weight rows (a unit) against the
+// activation: K = 2048 with the lane's 64-element fp16 activation slice in
+// registers (xh: 32 half pairs), or any K with the activation in shared
+// memory.  After the butterfly every lane holds both sums.
+__device__ __forceinline__ void dot2_regs(const half* r0, const half* r1, const uint32_t* xh, int lane, float& s0,
                                           float& s1) {
     float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const uint4 w0 = *reinterpret_cast<const uint4*>(r0 + 256 * j + 8 * lane);
         const uint4 w1 = *reinterpret_cast<const uint4*>(r1 + 256 * j + 8 * lane);
-        float f0[8], f1[8];
-        unpack8(w0, f0);
-        unpack8(w1, f1);
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            a0 = __fmaf_rn(f0[e], xr[8 * j + e], a0);
-            a1 = __fmaf_rn(f0[e + 1], xr[8 * j + e + 1], a1);
-            b0 = __fmaf_rn(f1[e], xr[8 * j + e], b0);
-            b1 = __fmaf_rn(f1[e + 1], xr[8 * j + e + 1], b1);
-        }
+        fma2_f16(a0, a1, w0.x, xh[4 * j + 0]);
+        fma2_f16(b0, b1, w1.x, xh[4 * j + 0]);
+        fma2_f16(a0, a1, w0.y, xh[4 * j + 1]);
+        fma2_f16(b0, b1, w1.y, xh[4 * j + 1]);
+        fma2_f16(a0, a1, w0.z, xh[4 * j + 2]);
+        fma2_f16(b0, b1, w1.z, xh[4 * j + 2]);
+        fma2_f16(a0, a1, w0.w, xh[4 * j + 3]);
+        fma2_f16(b0, b1, w1.w, xh[4 * j + 3]);
     }
     s0 = a0 + a1;
     s1 = b0 + b1;
@@ -91,17 +101,14 @@ __device__ __forceinline__ void dot2_smem(const half* r0, const half* r1, const 
         const uint4 w0 = *reinterpret_cast<const uint4*>(r0 + k);
         const uint4 w1 = *reinterpret_cast<const uint4*>(r1 + k);
         const uint4 xv = *reinterpret_cast<const uint4*>(xs + k);
-        float f0[8], f1[8], xf[8];
-        unpack8(w0, f0);
-        unpack8(w1, f1);
-        unpack8(xv, xf);
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            a0 = __fmaf_rn(f0[e], xf[e], a0);
-            a1 = __fmaf_rn(f0[e + 1], xf[e + 1], a1);
-            b0 = __fmaf_rn(f1[e], xf[e], b0);
-            b1 = __fmaf_rn(f1[e + 1], xf[e + 1], b1);
-        }
+        fma2_f16(a0, a1, w0.x, xv.x);
+        fma2_f16(b0, b1, w1.x, xv.x);
+        fma2_f16(a0, a1, w0.y, xv.y);
+        fma2_f16(b0, b1, w1.y, xv.y);
+        fma2_f16(a0, a1, w0.z, xv.z);
+        fma2_f16(b0, b1, w1.z, xv.z);
+        fma2_f16(a0, a1, w0.w, xv.w);
+        fma2_f16(b0, b1, w1.w, xv.w);
     }
     s0 = a0 + a1;
     s1 = b0 + b1;
@@ -305,7 +312,7 @@ __device__ bool grid_sync(const DecodeArgs& a, Smem& s, uint32_t& nbar, int tid,
 // embedding) or flag-carrying words with `tag`.  Returns the CTA-wide failure
 // verdict (true = a wait expired somewhere in the CTA).
 __device__ bool load_norm(const DecodeArgs& a, const half* plain, const unsigned long long* ll, uint32_t tag,
-                          const half* w, Smem& s, int tid, float* xr, bool bad, int& np) {
+                          const half* w, Smem& s, int tid, uint32_t* xr, bool bad, int& np) {
     const uint4 wv = *reinterpret_cast<const uint4*>(w + tid * 8);  // in flight while polling
     uint4 v;
     if (plain) {
@@ -329,7 +336,10 @@ __device__ bool load_norm(const DecodeArgs& a, const half* plain, const unsigned
     named_bar_sync(1, 256);
     const int lane = tid & 31;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) unpack8(*reinterpret_cast<const uint4*>(s.xs + 256 * j + 8 * lane), xr + 8 * j);
+    for (int j = 0; j < 8; ++j) {
+        const uint4 q = *reinterpret_cast<const uint4*>(s.xs + 256 * j + 8 * lane);
+        xr[4 * j] = q.x; xr[4 * j + 1] = q.y; xr[4 * j + 2] = q.z; xr[4 * j + 3] = q.w;
+    }
     return false;
 }
 
@@ -389,7 +399,7 @@ __device__ __forceinline__ void epilogue(int ph, const DecodeArgs& a, const Smem
 // Phases run through one call site so the kernel's code stays small enough
 // for the instruction caches (the phase id selects range, dot and epilogue).
 __device__ __forceinline__ void gemv_phase(int PH, const DecodeArgs& a, Smem& s, StepCtx& c, uint32_t& chunk,
-                                           const float* xr, int warp, int lane, bool& bad, Feed& feed,
+                                           const uint32_t* xr, int warp, int lane, bool& bad, Feed& feed,
                                            uint64_t pol) {
     const int R = PH == PH_LM ? 4 : PH == PH_C ? 3 : PH == PH_W12 ? 2 : PH == PH_O ? 1 : 0;
     const int u0 = s.range[R][0], u1 = s.range[R][1], CH = s.range[R][2], K = s.range[R][3];
@@ -590,7 +600,7 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
     uint32_t chunk = 0, nbar = 0;
     int token = a.first_token;
     StepCtx c;
-    float xr[64];
+    uint32_t xr[32];  // this lane's 64 fp16 activation values of the current phase
     c.ipt = (a.V + 511) / 512;
     const Tags tags{a.flag_base, a.NL};
     bool bad = false;
@@ -635,8 +645,10 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
                 *reinterpret_cast<uint4*>(s.xs + 8 * tid) = make_uint4(d[0], d[1], d[2], d[3]);
                 named_bar_sync(1, 256);
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    unpack8(*reinterpret_cast<const uint4*>(s.xs + 256 * j + 8 * lane), xr + 8 * j);
+                for (int j = 0; j < 8; ++j) {
+                    const uint4 q = *reinterpret_cast<const uint4*>(s.xs + 256 * j + 8 * lane);
+                    xr[4 * j] = q.x; xr[4 * j + 1] = q.y; xr[4 * j + 2] = q.z; xr[4 * j + 3] = q.w;
+                }
             } else if (ph == PH_C) {
                 // SwiGLU output into s.act.  s.act was last read by the previous
                 // layer's C phase, which every warp has left (several named

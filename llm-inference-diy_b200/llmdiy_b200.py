@@ -18,6 +18,7 @@ import re
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_build", "libllmdiy_b200.so")
+LIB_PATH = os.environ.get("LLMDIY_LIB", LIB_PATH)  # an alternative build of the library (A/B timing)
 DRIVER_PATH = os.path.join(_HERE, "_build", "qwen_infer_b200")
 INCLUDE_DIR = os.path.join(os.path.dirname(_HERE), "include")
 
