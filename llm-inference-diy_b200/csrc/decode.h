@@ -64,12 +64,11 @@ struct LayerPtrs {
 // store; a reader polls exactly the words it needs until they carry the tag
 // of the phase instance it expects.  Tags are unique per (launch, step,
 // layer, phase), so no buffer ever needs clearing between phases.
-enum LLSlot : uint32_t { LL_QKV = 0, LL_ATT = 1, LL_XO = 2, LL_ACT = 3, LL_XC = 4, LL_PER_LAYER = 5 };
+enum LLSlot : uint32_t { LL_QKV = 0, LL_ATT = 1, LL_XO = 2, LL_ACT = 3, LL_XC = 4, LL_APART = 5, LL_PER_LAYER = 6 };
 
 // Per-launch control words, zeroed by the host before every launch.
 struct DecodeControl {
     unsigned int bar;                  // grid barrier arrivals
-    unsigned int head_ctr[kHeads];     // attention-merge arrivals per head
     int err;                           // first error code (0 = none)
     int err_where;                     // diagnostic: phase id of the failure
     int n_done;                        // steps completed
@@ -90,8 +89,8 @@ struct DecodeArgs {
     unsigned long long* ll_xo;   // [H/2]  residual stream after o_proj
     unsigned long long* ll_act;  // [IM]   SwiGLU output, one value per word
     unsigned long long* ll_xc;   // [H/2]  residual stream after c_proj
+    unsigned long long* ll_apart;  // [kHeads][kAttnSplits][130] split partials (o[128], m, l) as fp32 words
     uint32_t flag_base;          // tag of this launch's first phase instance minus 1
-    float* att_part;          // [kHeads * kAttnSplits * 130] split partials (o[128], m, l)
     DecodeControl* ctl;
     int* tokens_out;          // [n_steps] device copy of generated tokens (may be null)
     int* host_tokens;         // mapped host buffer for streaming (may be null)

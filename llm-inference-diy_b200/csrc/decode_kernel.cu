@@ -157,6 +157,27 @@ __device__ __forceinline__ bool ll_read(const unsigned long long* p, int stride,
     return false;
 }
 
+// As ll_read for the first n <= N of the N words (the rest are not touched).
+template <int N>
+__device__ __forceinline__ bool ll_read_n(const unsigned long long* p, int stride, int n, uint32_t tag, uint32_t* out) {
+    uint32_t pending = (n >= 32) ? 0xffffffffu : ((1u << n) - 1u);
+    for (uint32_t it = 0; it < kPollLimit; ++it) {
+        unsigned long long v[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) v[i] = (i < n) ? ll_load(p + (size_t)i * stride) : 0ull;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            if ((pending & (1u << i)) && (uint32_t)(v[i] >> 32) == tag) {
+                out[i] = (uint32_t)v[i];
+                pending &= ~(1u << i);
+            }
+        }
+        if (!pending) return true;
+        __nanosleep(it < 8 ? 32 : 128);
+    }
+    return false;
+}
+
 // The SwiGLU output (one fp16 per word, IM <= kMaxIM words): thread tid
 // gathers words tid, tid+256, ... into out[] (shared memory), 12 loads in
 // flight per round.
@@ -552,44 +573,71 @@ __device__ bool attention_phase(const DecodeArgs& a, Smem& s, const StepCtx& c, 
     }
     if (named_bar_or(1, 256, bad)) return true;
     if (!active) return false;
-    float* part = a.att_part + (size_t)(h * S + sp) * 130;
+    // This CTA's partial (o[128] normalised by nothing, m, l) over its rows.
+    const uint32_t tp = tags(c.step, c.layer, LL_APART);
+    float acc = 0.f, Ls = 0.f, M = -INFINITY;
     if (tid < kHeadDim) {
-        float M = -INFINITY;
         for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, s.sm[w]);
-        float Ls = 0.f, acc = 0.f;
         for (int w = 0; w < kConsumerWarps; ++w) {
             if (s.sm[w] == -INFINITY) continue;
             const float f = __expf(s.sm[w] - M);
             Ls += s.sl[w] * f;
             acc += s.so[w][tid] * f;
         }
-        part[tid] = acc;
-        if (tid == 0) { part[128] = M; part[129] = Ls; }
     }
-    named_bar_sync(1, 256);
-    if (tid == 0) {
-        __threadfence();
-        const unsigned int old = atomicAdd(&a.ctl->head_ctr[h], 1u);
-        s.last = ((old + 1u) % (unsigned)S) == 0u;
-        __threadfence();
-    }
-    named_bar_sync(1, 256);
-    if (s.last && tid < kHeadDim / 2) {
-        // merge; thread j produces dims (2j, 2j+1) of head h as one word
-        const float* base = a.att_part + (size_t)h * S * 130;
-        float M = -INFINITY;
-        for (int j = 0; j < S; ++j) M = fmaxf(M, __ldcg(base + j * 130 + 128));
-        float Ls = 0.f, acc0 = 0.f, acc1 = 0.f;
-        for (int j = 0; j < S; ++j) {
-            const float mj = __ldcg(base + j * 130 + 128);
-            if (mj == -INFINITY) continue;
-            const float f = __expf(mj - M);
-            Ls += __ldcg(base + j * 130 + 129) * f;
-            acc0 += __ldcg(base + j * 130 + 2 * tid) * f;
-            acc1 += __ldcg(base + j * 130 + 2 * tid + 1) * f;
+    unsigned long long* part = a.ll_apart + (size_t)h * S * 130;
+    if (sp != 0) {
+        // publish as flag-carrying words; split 0 of the head merges
+        if (tid < kHeadDim) ll_store(part + sp * 130 + tid, __float_as_uint(acc), tp);
+        if (tid == 0) {
+            ll_store(part + sp * 130 + 128, __float_as_uint(M), tp);
+            ll_store(part + sp * 130 + 129, __float_as_uint(Ls), tp);
         }
-        const float inv = __frcp_rn(Ls);
-        const half2 r = __floats2half2_rn(acc0 * inv, acc1 * inv);
+        return false;
+    }
+    // split 0: gather the other splits' partials into shared memory (s.so rows
+    // 0..S-2 hold o of splits 1..S-1, s.sm / s.sl their m and l), then merge
+    named_bar_sync(1, 256);  // every warp is done reading s.so / s.sm / s.sl
+    static_assert(kAttnSplits - 1 <= kConsumerWarps, "one shared row per other split");
+    {
+        constexpr int kWords = (S - 1) * 130, kPer = (kWords + kDecodeThreads - 1) / kDecodeThreads;
+        const int n = (kWords - tid + kDecodeThreads - 1) / kDecodeThreads;
+        uint32_t d[kPer];
+        bad |= !ll_read_n<kPer>(part + 130 + tid, kDecodeThreads, n, tp, d);
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            if (k >= n) break;
+            const int i = tid + k * kDecodeThreads, j = i / 130, e = i % 130;
+            const float v = __uint_as_float(d[k]);
+            if (e < kHeadDim) s.so[j][e] = v;
+            else if (e == kHeadDim) s.sm[j] = v;
+            else s.sl[j] = v;
+        }
+    }
+    if (named_bar_or(1, 256, bad)) return true;
+    if (tid < kHeadDim) {
+        // merge in split order: own partial first, then splits 1..S-1
+        float Mx = M;
+        for (int j = 0; j < S - 1; ++j) Mx = fmaxf(Mx, s.sm[j]);
+        float L2 = 0.f, o = 0.f;
+        if (M != -INFINITY) {
+            const float f = __expf(M - Mx);
+            L2 += Ls * f;
+            o += acc * f;
+        }
+        for (int j = 0; j < S - 1; ++j) {
+            if (s.sm[j] == -INFINITY) continue;
+            const float f = __expf(s.sm[j] - Mx);
+            L2 += s.sl[j] * f;
+            o += s.so[j][tid] * f;
+        }
+        const float r = o * __frcp_rn(L2);
+        // dims (2i, 2i+1) travel as one word: pair up through shared memory
+        s.so[kConsumerWarps - 1][tid] = r;
+    }
+    named_bar_sync(1, 256);
+    if (tid < kHeadDim / 2) {
+        const half2 r = __floats2half2_rn(s.so[kConsumerWarps - 1][2 * tid], s.so[kConsumerWarps - 1][2 * tid + 1]);
         ll_store(a.ll_att + h * 64 + tid, *reinterpret_cast<const uint32_t*>(&r), tags(c.step, c.layer, LL_ATT));
     }
     return false;

@@ -78,7 +78,6 @@ struct llmdiy_engine {
     half* kc = nullptr;
     half* vc = nullptr;
     half *x = nullptr, *logits = nullptr;
-    float* att_part = nullptr;
     unsigned long long* ll = nullptr;  // flag-carrying words: qkv | att | xo | act | xc
     size_t ll_words = 0;
     uint32_t tag_base = 0;
@@ -246,11 +245,10 @@ int alloc_state(llmdiy_engine* e) {
     CK(cudaMalloc(&e->kc, kv * 2), "cudaMalloc K cache");
     CK(cudaMalloc(&e->vc, kv * 2), "cudaMalloc V cache");
     CK(cudaMalloc(&e->x, H * 2), "alloc x");
-    e->ll_words = 3 * H / 2 + H / 2 + H / 2 + c.intermediate_size + H / 2;
+    e->ll_words = 3 * H / 2 + H / 2 + H / 2 + c.intermediate_size + H / 2 + (size_t)kHeads * kAttnSplits * 130;
     CK(cudaMalloc(&e->ll, e->ll_words * 8), "alloc flag words");
     CK(cudaMemset(e->ll, 0, e->ll_words * 8), "clear flag words");
     CK(cudaMalloc(&e->logits, (size_t)c.vocab_size * 2), "alloc logits");
-    CK(cudaMalloc(&e->att_part, sizeof(float) * kHeads * kAttnSplits * 130), "alloc partials");
     CK(cudaMalloc(&e->ctl, sizeof(DecodeControl)), "alloc control");
     CK(cudaMalloc(&e->tokens_dev, sizeof(int) * (c.max_seqlen + 1)), "alloc tokens");
     CK(cudaMalloc(&e->forced_dev, sizeof(int) * (c.max_seqlen + 1)), "alloc forced");
@@ -343,6 +341,7 @@ int launch(llmdiy_engine* e, int first_token, int pos0, int n_steps, bool skip_l
     a.ll_xo = a.ll_att + H / 2;
     a.ll_act = a.ll_xo + H / 2;
     a.ll_xc = a.ll_act + c.intermediate_size;
+    a.ll_apart = a.ll_xc + H / 2;
     // tags are unique per phase instance across launches; on wrap-around the
     // words are cleared so no stale word can carry a future tag
     const uint32_t need = decode_tags_per_launch(n_steps, (int)c.num_layers);
@@ -352,7 +351,6 @@ int launch(llmdiy_engine* e, int first_token, int pos0, int n_steps, bool skip_l
     }
     a.flag_base = e->tag_base;
     e->tag_base += need;
-    a.att_part = e->att_part;
     a.ctl = e->ctl;
     a.tokens_out = e->tokens_dev;
     a.host_tokens = stream_host ? e->host_tokens_dev : nullptr;
@@ -473,7 +471,6 @@ void llmdiy_engine_destroy(llmdiy_engine* e) {
     cudaFree(e->x);
     cudaFree(e->ll);
     cudaFree(e->logits);
-    cudaFree(e->att_part);
     cudaFree(e->ctl);
     cudaFree(e->tokens_dev);
     cudaFree(e->forced_dev);
