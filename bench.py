@@ -312,6 +312,123 @@ def run_ours(args, rank, world, local, pg):
     eng.close()
 
 
+# ------------------------------------------------------------------ flash-decoding op (configs 1 and 5)
+FD_HEADS, FD_STRIDE = 16, 2048
+
+
+def fd_bytes(L):
+    """Algorithmic bytes of one multi-head decode-attention call: K and V rows read, q read, O written."""
+    return 2 * L * FD_HEADS * 128 * 2 + 2 * FD_HEADS * 128 * 2
+
+
+def run_fd_op(args, rank, world, local, pg):
+    """Config 1 (L=1024) and config 5 (L=131072 split over the ranks' GPUs): 16 heads x 128, one query
+    token, K/V ~ N(0,1) fp16 in the engine cache layout.  Config 1 rotates over enough K/V copies
+    (> 2x L2) that every call reads from HBM, and times a CUDA graph of the calls; config 5 shards
+    the 131072 positions contiguously over the ranks (each rank's partials -> NCCL all-gather ->
+    LSE merge) and times on device with the max over ranks."""
+    import torch
+    import llmdiy_b200 as L
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    peak, peak_kind = measured_peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    lines = []
+    if world == 1:
+        # ---- config 1: 16 x 128, L = 1024
+        Lc = 1024
+        nset = 40  # 40 x 8.4 MB = 336 MB > 2 x L2
+        q = torch.randn(FD_HEADS * 128, generator=g, device=dev).half()
+        Ks = [torch.randn(Lc * FD_STRIDE, generator=g, device=dev).half() for _ in range(nset)]
+        Vs = [torch.randn(Lc * FD_STRIDE, generator=g, device=dev).half() for _ in range(nset)]
+        O = torch.empty(FD_HEADS * 128, dtype=torch.float16, device=dev)
+        nb = L.fd_mh_work_bytes(Lc, FD_HEADS)
+        work = torch.empty((nb + 3) // 4, dtype=torch.float32, device=dev)
+        st = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(st):
+            for i in range(nset):  # warm-up (also loads the module)
+                L.fd_multihead(q.data_ptr(), Ks[i].data_ptr(), Vs[i].data_ptr(), O.data_ptr(), Lc, FD_STRIDE,
+                               FD_HEADS, work.data_ptr(), nb, stream=st.cuda_stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            for i in range(nset):
+                L.fd_multihead(q.data_ptr(), Ks[i].data_ptr(), Vs[i].data_ptr(), O.data_ptr(), Lc, FD_STRIDE,
+                               FD_HEADS, work.data_ptr(), nb, stream=st.cuda_stream)
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(1, args.steps)
+        e0.record(st)
+        with torch.cuda.stream(st):
+            for _ in range(reps):
+                graph.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / (reps * nset)
+        gbs = fd_bytes(Lc) / (us * 1e-6) / 1e9
+        lines.append({"metric": "flash_decode_GBps", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
+                      "us_per_call": round(us, 3), "higher_is_better": True, "dtype": "fp16 (fp32 accumulate)",
+                      "data": "synthetic N(0,1)", "config": {"workload": "BASELINE configs[0]: 16x128, L=1024, "
+                      "engine layout stride 2048", "l2": f"cold: {nset} K/V copies rotated, CUDA graph of the calls"},
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                                   "frac": round(gbs / peak, 4), "peak_kind": peak_kind}})
+        del graph, Ks, Vs
+        torch.cuda.empty_cache()
+    # ---- config 5: L = 131072 over the ranks
+    Lt = 131072
+    Lr = Lt // world
+    q = torch.randn(FD_HEADS * 128, generator=g, device=dev).half()
+    if pg is not None:
+        pg.broadcast(q, src=0)
+    K = torch.randn(Lr * FD_STRIDE, generator=g, device=dev).half()
+    V = torch.randn(Lr * FD_STRIDE, generator=g, device=dev).half()
+    O = torch.empty(FD_HEADS * 128, dtype=torch.float16, device=dev)
+    nb = L.fd_mh_work_bytes(Lr, FD_HEADS)
+    work = torch.empty((nb + 3) // 4, dtype=torch.float32, device=dev)
+    part = torch.empty((FD_HEADS, 130), dtype=torch.float32, device=dev)
+    parts = torch.empty((world, FD_HEADS, 130), dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def call():
+        if world == 1:
+            L.fd_multihead(q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), Lr, FD_STRIDE, FD_HEADS,
+                           work.data_ptr(), nb, stream=st.cuda_stream)
+        else:
+            L.fd_mh_partials(q.data_ptr(), K.data_ptr(), V.data_ptr(), Lr, FD_STRIDE, FD_HEADS, part.data_ptr(),
+                             work.data_ptr(), nb, stream=st.cuda_stream)
+            pg.all_gather_into_tensor(parts, part)
+            L.fd_mh_merge(parts.data_ptr(), world, FD_HEADS, O.data_ptr(), stream=st.cuda_stream)
+
+    for _ in range(max(3, args.warmup)):
+        call()
+    barrier(pg, local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(1, args.steps) * 4
+    e0.record(st)
+    for _ in range(reps):
+        call()
+    e1.record(st)
+    torch.cuda.synchronize()
+    barrier(pg, local)
+    ms = max_over_ranks(pg, e0.elapsed_time(e1) / reps, local)
+    gbs = fd_bytes(Lt) / (ms * 1e-3) / 1e9
+    assert L.fd_mh_status(work.data_ptr(), Lr, FD_HEADS) == 0
+    lines.append({"metric": "flash_decode_GBps", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world,
+                  "us_per_call": round(ms * 1000, 2), "higher_is_better": True, "scaling": "strong",
+                  "dtype": "fp16 (fp32 accumulate)", "data": "synthetic N(0,1)",
+                  "config": {"workload": "BASELINE configs[4]: 16x128, L=131072 split over the GPUs",
+                             "rows_per_gpu": Lr, "exchange": "NCCL all-gather of 16x130 fp32 per rank"
+                             if world > 1 else "none", "l2": "inputs larger than L2 (1 GiB of K+V)"},
+                  "roofline": {"bound": "hbm", "achieved_per_gpu": round(gbs / world, 1), "peak": peak,
+                               "unit": "GB/s", "frac": round(gbs / world / peak, 4), "peak_kind": peak_kind}})
+    if rank == 0:
+        for ln in lines:
+            print(json.dumps(ln), flush=True)
+
+
 def run_ncu_case():
     """Small case for ncu captures of decode_kernel: the Qwen-1.8B shapes with 4 layers (full vocab,
     0.95 GB of weights, larger than L2), one prefill launch of 127 tokens, then one decode launch of
@@ -341,13 +458,22 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", action="store_true", help="run the small decode case used for ncu captures")
+    ap.add_argument("--workload", default="decode", choices=["decode", "fd-op"],
+                    help="decode: the headline config-2 line; fd-op: flash-decoding op lines (configs 1 and 5)")
     args = ap.parse_args()
     if args.ncu_case:
         run_ncu_case()
         return
     rank, world, local, pg = dist_setup(args.gpus)
     try:
-        if args.impl == "reference":
+        if args.workload == "fd-op":
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "workload": "fd-op", "unavailable":
+                                      "the reference has no CPU flash-decoding path; see the decode arm"}))
+            else:
+                run_fd_op(args, rank, world, local, pg)
+        elif args.impl == "reference":
             run_reference(args, rank, world)
         else:
             run_ours(args, rank, world, local, pg)

@@ -52,6 +52,26 @@ int llmdiy_fd_v5_split_stage1(const uint16_t* Q, const uint16_t* K, const uint16
  * <<<1,128>>> (qwen_infer.cu:674-676). */
 int llmdiy_fd_opt_stage2(const uint16_t* Opart, const float* LSE, uint16_t* O, int num_chunks, void* stream);
 
+/* ---- multi-head split-KV flash decoding (new entry points: the reference attends one head per
+ * launch with fd_v5_split_stage1 + fd_opt_stage2, kernels/flash_decode_q1_opt.cuh:548-724, called per
+ * head at qwen_infer.cu:650-677).  Q is [num_heads][128] fp16; K and V are the engine's cache layout,
+ * row r of head h at r*stride + h*128 (stride >= num_heads*128, a multiple of 8); O is [num_heads][128].
+ * Scale 1/sqrt(128), fp32 accumulation, fast-math exponentials like the reference.  `work` is caller
+ * scratch of llmdiy_fd_mh_work_bytes(L, num_heads) bytes (device memory, 16-byte aligned); nothing is
+ * allocated.  A partial is 130 fp32: o[128] (unnormalised), m (max score), l (sum of e^{s-m}). */
+size_t llmdiy_fd_mh_work_bytes(int L, int num_heads);
+/* O = softmax(q k^T / sqrt(128)) v for every head over rows [0, L). */
+int llmdiy_fd_multihead(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int L, int stride,
+                        int num_heads, float* work, size_t work_bytes, void* stream);
+/* One merged partial per head over rows [0, L) of this K/V shard: part is [num_heads][130] fp32. */
+int llmdiy_fd_mh_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride,
+                          int num_heads, float* part, float* work, size_t work_bytes, void* stream);
+/* Log-sum-exp merge of G shards' partials, parts = [G][num_heads][130] in shard order, into O. */
+int llmdiy_fd_mh_merge(const float* parts, int G, int num_heads, uint16_t* O, void* stream);
+/* After the stream is synchronised: 0, or -5 when a pipeline wait of the last call with this
+ * workspace expired (its output is then not valid). */
+int llmdiy_fd_mh_status(const float* work, int L, int num_heads);
+
 /* No counterpart in the reference.  Split-KV flash decoding of one head in a single launch that
  * allocates nothing: the same result, bit for bit, as llmdiy_fd_v5_split_stage1 + llmdiy_fd_opt_stage2
  * with num_chunks = ceil(L/256), but the chunk partials live in a file-scope device array (33,536 bytes)

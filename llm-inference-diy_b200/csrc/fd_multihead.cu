@@ -1,0 +1,430 @@
+// fd_multihead.cu — multi-head split-KV flash decoding (one query token).
+//
+// The reference attends one head per launch (fd_v5_split_stage1_kernel +
+// fd_opt_stage2_kernel, kernels/flash_decode_q1_opt.cuh:548-724, launched per
+// head at qwen_infer.cu:650-677).  Here all heads and all KV positions go in
+// one launch: CTA (split, head) streams its rows of K and V for that head
+// through a 4-stage shared-memory pipeline of 64-row TMA tiles (2-D tensor
+// maps over the [L][stride] cache, box 128 x 64), keeps an online softmax
+// state per half-warp, and writes its unnormalised partial (o[128], m, l) in
+// fp32.  A second kernel merges each head's partials (log-sum-exp) into the
+// fp16 output or into one fp32 partial per head — the form the multi-GPU path
+// exchanges (NCCL all-gather) before the final merge of the shards' partials.
+#include <cuda.h>
+#include <algorithm>
+#include <mutex>
+
+#include "../../include/llmdiy_kernels.h"
+#include "ops.cuh"
+
+using namespace llmdiy;
+
+namespace {
+
+constexpr int kFdHeadDim = 128;
+constexpr int kFdRows = 64;  // rows per TMA tile
+constexpr int kFdStages = 6;
+constexpr int kFdThreads = 128;  // 4 warps x 16 rows of a tile
+constexpr int kFdPart = kFdHeadDim + 2;
+constexpr int kFdTileBytes = kFdRows * kFdHeadDim * 2;
+
+constexpr int kFdMergeMax = 1024;  // most partials one merge combines
+
+struct FdSmem {
+    half k[kFdStages][kFdRows * kFdHeadDim];
+    half v[kFdStages][kFdRows * kFdHeadDim];
+    uint64_t full[kFdStages];
+    float so[4][kFdHeadDim];
+    float sm[4], sl[4];
+};
+
+// Log-sum-exp merge of n partials of one head by the 128 threads of a CTA, in
+// order j = 0..n-1: O = sum_j e^{m_j - M} o_j / sum_j e^{m_j - M} l_j.  Partial
+// j is at p + j * jstride (floats).  Partials are staged through shared memory
+// (`scratch`, cap floats) in batches with coalesced, independent loads, so a
+// batch costs one L2 round trip.  Writes the fp16 output and/or the merged
+// fp32 partial (o unnormalised, M, L).
+__device__ __forceinline__ void fd_merge_head(const float* p, int n, int jstride, float* scratch, int cap,
+                                              float* red, half* O, float* out_part) {
+    const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+    float mx = -INFINITY;
+    for (int j = d; j < n; j += kFdHeadDim) mx = fmaxf(mx, __ldcg(p + (size_t)j * jstride + kFdHeadDim));
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const int per = cap / kFdPart;
+    float Ls = 0.f, acc = 0.f;
+    for (int j0 = 0; j0 < n; j0 += per) {
+        const int nb = min(per, n - j0);
+#pragma unroll 4
+        for (int i = d; i < nb * kFdPart; i += kFdHeadDim) {
+            const int j = i / kFdPart, e = i - j * kFdPart;
+            scratch[i] = __ldcg(p + (size_t)(j0 + j) * jstride + e);
+        }
+        __syncthreads();
+        for (int j = 0; j < nb; ++j) {
+            const float mj = scratch[j * kFdPart + kFdHeadDim];
+            const float f = mj == -INFINITY ? 0.f : __expf(mj - M);
+            Ls = __fmaf_rn(scratch[j * kFdPart + kFdHeadDim + 1], f, Ls);
+            acc = __fmaf_rn(f, scratch[j * kFdPart + d], acc);
+        }
+        __syncthreads();
+    }
+    if (O) O[d] = f2h(acc * __frcp_rn(Ls));
+    if (out_part) {
+        out_part[d] = acc;
+        if (d == 0) { out_part[kFdHeadDim] = M; out_part[kFdHeadDim + 1] = Ls; }
+    }
+}
+
+// Persistent: CTA b takes work items (head, split) b, b + grid, ... and its
+// TMA pipeline runs across item boundaries, so the next item's tiles are
+// already in flight when one item ends.  Item i: head i / S, split i % S,
+// rows [split * rows_per_split, min(L, (split + 1) * rows_per_split)).
+struct FdCursor {
+    int item, tile, ntiles, r0;  // current item, tile within it, its tile count and first row
+};
+
+__device__ __forceinline__ void fd_item(int item, int S, int L, int rows_per_split, FdCursor& c) {
+    c.item = item;
+    c.tile = 0;
+    const int sp = item % S;
+    c.r0 = sp * rows_per_split;
+    const int r1 = min(L, c.r0 + rows_per_split);
+    c.ntiles = r1 > c.r0 ? (r1 - c.r0 + kFdRows - 1) / kFdRows : 0;
+}
+
+__global__ void __launch_bounds__(kFdThreads, 1)
+    fd_partials_k(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                  const half* __restrict__ Q, int L, int S, int H, int rows_per_split, float* __restrict__ part,
+                  int* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    FdSmem& s = *reinterpret_cast<FdSmem*>(smem_raw);
+    const int tid = threadIdx.x, G = gridDim.x, nitems = S * H;
+    const int warp = tid >> 5, lane = tid & 31, hw = lane >> 4, dl = (lane & 15) * 8;
+    const uint64_t pol = l2_policy_evict_first();
+    if (tid == 0) {
+        for (int i = 0; i < kFdStages; ++i) mbar_init(&s.full[i], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    // producer cursor (thread 0) and the count of tiles issued / consumed in this CTA's sequence
+    FdCursor pc;
+    fd_item(blockIdx.x, S, L, rows_per_split, pc);
+    uint32_t issued = 0, consumed = 0;
+    auto produce = [&]() {  // issue the next tile of the sequence, if any
+        while (pc.item < nitems && pc.tile >= pc.ntiles) fd_item(pc.item + G, S, L, rows_per_split, pc);
+        if (pc.item >= nitems) return;
+        const int st = issued % kFdStages, h = pc.item / S, y = pc.r0 + pc.tile * kFdRows;
+        mbar_arrive_expect_tx(&s.full[st], 2 * kFdTileBytes);
+        tma_load_2d_hint(s.k[st], &tk, h * kFdHeadDim, y, &s.full[st], pol);
+        tma_load_2d_hint(s.v[st], &tv, h * kFdHeadDim, y, &s.full[st], pol);
+        ++pc.tile;
+        ++issued;
+    };
+    if (tid == 0)
+        for (int i = 0; i < kFdStages; ++i) produce();
+    const float scale = __frcp_rn(sqrtf((float)kFdHeadDim));
+    bool failed = false;
+    for (int item = blockIdx.x; item < nitems && !failed; item += G) {
+        FdCursor cc;
+        fd_item(item, S, L, rows_per_split, cc);
+        const int h = item / S;
+        const int r1 = min(L, cc.r0 + rows_per_split);
+        float q8[8];
+        unpack8(*reinterpret_cast<const uint4*>(Q + (size_t)h * kFdHeadDim + dl), q8);
+        float m = -INFINITY, l = 0.f, o8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o8[e] = 0.f;
+        for (int t = 0; t < cc.ntiles; ++t, ++consumed) {
+            const int st = consumed % kFdStages;
+            const bool ok = mbar_wait(&s.full[st], (consumed / kFdStages) & 1);
+            if (__syncthreads_or(!ok)) {
+                failed = true;
+                break;
+            }
+            const int nvalid = min(kFdRows, r1 - (cc.r0 + t * kFdRows));
+            const half* kt = s.k[st];
+            const half* vt = s.v[st];
+            float sc[8];
+            uint4 vr[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int r = warp * 16 + 2 * j + hw;
+                float kf[8];
+                unpack8(*reinterpret_cast<const uint4*>(kt + r * kFdHeadDim + dl), kf);
+                vr[j] = *reinterpret_cast<const uint4*>(vt + r * kFdHeadDim + dl);
+                float d = 0.f;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) d = __fmaf_rn(q8[e], kf[e], d);
+                sc[j] = d;
+            }
+#pragma unroll
+            for (int mk = 8; mk >= 1; mk >>= 1)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], mk);
+            float mx = m;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const bool valid = warp * 16 + 2 * j + hw < nvalid;
+                sc[j] = valid ? sc[j] * scale : -INFINITY;
+                mx = fmaxf(mx, sc[j]);
+            }
+            if (mx != -INFINITY) {
+                const float corr = __expf(m - mx);
+                l *= corr;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) o8[e] *= corr;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float p = __expf(sc[j] - mx);
+                    l += p;
+                    float vf[8];
+                    unpack8(vr[j], vf);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o8[e] = __fmaf_rn(p, vf[e], o8[e]);
+                }
+                m = mx;
+            }
+            __syncthreads();  // every warp is done with stage st: refill it
+            if (tid == 0) produce();
+        }
+        if (failed) break;
+        combine_halfwarps(m, l, o8);
+        if (lane < 16) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s.so[warp][dl + e] = o8[e];
+        }
+        if (lane == 0) { s.sm[warp] = m; s.sl[warp] = l; }
+        __syncthreads();
+        const int d = tid;
+        float M = -INFINITY;
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, s.sm[w]);
+        float Ls = 0.f, acc = 0.f;
+        for (int w = 0; w < 4; ++w) {
+            if (s.sm[w] == -INFINITY) continue;
+            const float f = __expf(s.sm[w] - M);
+            Ls += s.sl[w] * f;
+            acc = __fmaf_rn(f, s.so[w][d], acc);
+        }
+        float* p = part + (size_t)item * kFdPart;  // item = h * S + split
+        p[d] = acc;
+        if (d == 0) { p[kFdHeadDim] = M; p[kFdHeadDim + 1] = Ls; }
+        __syncthreads();  // s.so / s.sm / s.sl are reused by the next item
+    }
+    if (failed && tid == 0) {
+        atomicExch(err, 1);
+        // copies still in flight land in this CTA's shared memory: wait for them (bounded)
+        for (uint32_t i = consumed; i < issued; ++i) (void)mbar_wait(&s.full[i % kFdStages], (i / kFdStages) & 1);
+    }
+}
+
+// Merge of a head's S split partials (part = [H][S][130]) with 256 threads:
+// the weights e^{m_j - M} are computed once per partial, then thread group g
+// (threads g*128 .. g*128+127, one per dimension) sums partials j = g, g+2, ...
+// sixteen loads in flight at a time, and the two group sums are added.
+constexpr int kFdMergeThreads = 256;
+
+__global__ void __launch_bounds__(kFdMergeThreads)
+    fd_merge_splits_k(const float* __restrict__ part, int S, half* __restrict__ O, float* __restrict__ out_part) {
+    __shared__ float wgt[kFdMergeMax];
+    __shared__ float red[8], red2[8], acc2[kFdHeadDim];
+    const int h = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const float* p = part + (size_t)h * S * kFdPart;
+    float mx = -INFINITY;
+    for (int j = t; j < S; j += kFdMergeThreads) mx = fmaxf(mx, p[(size_t)j * kFdPart + kFdHeadDim]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    float M = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) M = fmaxf(M, red[w]);
+    float lsum = 0.f;
+    for (int j = t; j < S; j += kFdMergeThreads) {
+        const float mj = p[(size_t)j * kFdPart + kFdHeadDim];
+        const float f = mj == -INFINITY ? 0.f : __expf(mj - M);
+        wgt[j] = f;
+        lsum = __fmaf_rn(p[(size_t)j * kFdPart + kFdHeadDim + 1], f, lsum);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (lane == 0) red2[warp] = lsum;
+    __syncthreads();
+    float Ls = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) Ls += red2[w];
+    const int g = t >> 7, d = t & (kFdHeadDim - 1);
+    float acc = 0.f;
+    for (int j0 = g; j0 < S; j0 += 32) {
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const int j = j0 + 2 * k;
+            v[k] = j < S ? p[(size_t)j * kFdPart + d] : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const int j = j0 + 2 * k;
+            if (j < S) acc = __fmaf_rn(wgt[j], v[k], acc);
+        }
+    }
+    if (g == 1) acc2[d] = acc;
+    __syncthreads();
+    if (g == 0) {
+        acc += acc2[d];
+        if (O) O[(size_t)h * kFdHeadDim + d] = f2h(acc * __frcp_rn(Ls));
+        if (out_part) {
+            float* q = out_part + (size_t)h * kFdPart;
+            q[d] = acc;
+            if (d == 0) { q[kFdHeadDim] = M; q[kFdHeadDim + 1] = Ls; }
+        }
+    }
+}
+
+// Merge of G shards' partials (parts = [G][H][130]): one CTA per head.
+__global__ void __launch_bounds__(kFdHeadDim) fd_merge_ranks_k(const float* __restrict__ parts, int G, int H,
+                                                               half* __restrict__ O) {
+    __shared__ float scratch[8 * kFdPart];
+    __shared__ float red[4];
+    const int h = blockIdx.x;
+    fd_merge_head(parts + (size_t)h * kFdPart, G, H * kFdPart, scratch, 8 * kFdPart, red, O + (size_t)h * kFdHeadDim,
+                  nullptr);
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// Tensor map over one [L][stride] fp16 cache: box = 128 columns x 64 rows.
+bool make_map(CUtensorMap* m, const void* base, int L, int stride) {
+    EncodeTiled enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)stride, (cuuint64_t)L};
+    cuuint64_t strides[1] = {(cuuint64_t)stride * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kFdHeadDim, (cuuint32_t)kFdRows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int num_sms() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+// Split plan: rows per split (a multiple of the tile).  Items (head, split)
+// are spread over a persistent grid of one CTA per SM, so the plan aims at a
+// whole number of items per CTA with at most ~32 tiles (1 MB) per item.
+void plan(int L, int H, int* S, int* rows) {
+    const int tiles = (L + kFdRows - 1) / kFdRows;
+    const int sms = num_sms();
+    const long long total = (long long)tiles * H;
+    long long per_cta = (total + sms - 1) / sms;  // tiles per CTA if perfectly balanced
+    long long items_per_cta = (per_cta + 31) / 32;
+    if (items_per_cta < 1) items_per_cta = 1;
+    int s = (int)((items_per_cta * sms + H - 1) / H);
+    if (s > tiles) s = tiles;
+    if (s > kFdMergeMax) s = kFdMergeMax;
+    if (s < 1) s = 1;
+    const int tps = (tiles + s - 1) / s;
+    *rows = tps * kFdRows;
+    *S = (L + *rows - 1) / *rows;
+}
+
+int check_args(const void* Q, const void* K, const void* V, int L, int stride, int H) {
+    if (L <= 0 || H <= 0 || stride < H * kFdHeadDim || (stride & 7)) return (int)cudaErrorInvalidValue;
+    auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (!a16(Q) || !a16(K) || !a16(V)) return (int)cudaErrorInvalidValue;
+    return 0;
+}
+
+// Workspace: the split partials [H][S][130] fp32, then one error word
+// (cleared on the stream before every launch).
+size_t work_floats(int H, int S) { return (size_t)H * S * kFdPart + 4; }
+
+int launch_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride, int H, float* work,
+                    int S, int rows, uint16_t* O, float* out_part, cudaStream_t st) {
+    CUtensorMap tk, tv;
+    if (!make_map(&tk, K, L, stride) || !make_map(&tv, V, L, stride)) return (int)cudaErrorInvalidValue;
+    int* err = reinterpret_cast<int*>(work + (size_t)H * S * kFdPart);
+    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), st);
+    if (e != cudaSuccess) return (int)e;
+    static std::once_flag attr;
+    std::call_once(attr, [] {
+        cudaFuncSetAttribute(fd_partials_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(FdSmem));
+    });
+    const int grid = std::min(S * H, num_sms());
+    fd_partials_k<<<grid, kFdThreads, sizeof(FdSmem), st>>>(tk, tv, reinterpret_cast<const half*>(Q), L, S, H, rows,
+                                                             work, err);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+    fd_merge_splits_k<<<H, kFdMergeThreads, 0, st>>>(work, S, reinterpret_cast<half*>(O), out_part);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" size_t llmdiy_fd_mh_work_bytes(int L, int num_heads) {
+    if (L <= 0 || num_heads <= 0) return 0;
+    int S, rows;
+    plan(L, num_heads, &S, &rows);
+    return work_floats(num_heads, S) * sizeof(float);
+}
+
+extern "C" int llmdiy_fd_multihead(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int L,
+                                   int stride, int num_heads, float* work, size_t work_bytes, void* stream) {
+    int rc = check_args(Q, K, V, L, stride, num_heads);
+    if (rc) return rc;
+    int S, rows;
+    plan(L, num_heads, &S, &rows);
+    if (!O || !work || work_bytes < work_floats(num_heads, S) * sizeof(float)) return (int)cudaErrorInvalidValue;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    return launch_partials(Q, K, V, L, stride, num_heads, work, S, rows, O, nullptr, st);
+}
+
+extern "C" int llmdiy_fd_mh_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride,
+                                     int num_heads, float* part, float* work, size_t work_bytes, void* stream) {
+    int rc = check_args(Q, K, V, L, stride, num_heads);
+    if (rc) return rc;
+    int S, rows;
+    plan(L, num_heads, &S, &rows);
+    if (!part || !work || work_bytes < work_floats(num_heads, S) * sizeof(float)) return (int)cudaErrorInvalidValue;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    return launch_partials(Q, K, V, L, stride, num_heads, work, S, rows, nullptr, part, st);
+}
+
+extern "C" int llmdiy_fd_mh_merge(const float* parts, int G, int num_heads, uint16_t* O, void* stream) {
+    if (!parts || !O || G <= 0 || G > kFdMergeMax || num_heads <= 0) return (int)cudaErrorInvalidValue;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    fd_merge_ranks_k<<<num_heads, kFdHeadDim, 0, st>>>(parts, G, num_heads, reinterpret_cast<half*>(O));
+    return (int)cudaGetLastError();
+}
+
+extern "C" int llmdiy_fd_mh_status(const float* work, int L, int num_heads) {
+    if (!work || L <= 0 || num_heads <= 0) return (int)cudaErrorInvalidValue;
+    int S, rows;
+    plan(L, num_heads, &S, &rows);
+    int h = 0;
+    cudaError_t e = cudaMemcpy(&h, work + (size_t)num_heads * S * kFdPart, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return (int)e;
+    return h ? -5 : 0;
+}

@@ -71,6 +71,10 @@ def lib() -> ctypes.CDLL:
         "llmdiy_fd_v5_fused": [P, P, P, P, I, I, P],
         "llmdiy_fd_v5_split_stage1": [P, P, P, P, P, I, I, I, P],
         "llmdiy_fd_opt_stage2": [P, P, P, I, P],
+        "llmdiy_fd_multihead": [P, P, P, P, I, I, I, P, SZ, P],
+        "llmdiy_fd_mh_partials": [P, P, P, I, I, I, P, P, SZ, P],
+        "llmdiy_fd_mh_merge": [P, I, I, P, P],
+        "llmdiy_fd_mh_status": [P, I, I],
         "llmdiy_argmax": [P, P, I, P],
         "llmdiy_hgemv": [P, P, P, I, I, P],
         "llmdiy_hgemm_swizzle_nn": [P, P, P, I, I, I, P],
@@ -107,6 +111,8 @@ def lib() -> ctypes.CDLL:
     L.llmdiy_engine_destroy.restype = None
     L.llmdiy_engine_last_error.argtypes = [P]
     L.llmdiy_engine_last_error.restype = ctypes.c_char_p
+    L.llmdiy_fd_mh_work_bytes.argtypes = [I, I]
+    L.llmdiy_fd_mh_work_bytes.restype = SZ
     _lib = L
     return L
 
@@ -164,6 +170,28 @@ def fd_v5_split_stage1(Q, K, V, Opart, LSE, L, num_chunks, stride, stream=None):
 
 def fd_opt_stage2(Opart, LSE, O, num_chunks, stream=None):
     _check(lib().llmdiy_fd_opt_stage2(_p(Opart), _p(LSE), _p(O), num_chunks, _p(stream)), "fd_opt_stage2")
+
+
+def fd_mh_work_bytes(L, num_heads):
+    return int(lib().llmdiy_fd_mh_work_bytes(L, num_heads))
+
+
+def fd_multihead(Q, K, V, O, L, stride, num_heads, work, work_bytes, stream=None):
+    _check(lib().llmdiy_fd_multihead(_p(Q), _p(K), _p(V), _p(O), L, stride, num_heads, _p(work), work_bytes,
+                                     _p(stream)), "fd_multihead")
+
+
+def fd_mh_partials(Q, K, V, L, stride, num_heads, part, work, work_bytes, stream=None):
+    _check(lib().llmdiy_fd_mh_partials(_p(Q), _p(K), _p(V), L, stride, num_heads, _p(part), _p(work), work_bytes,
+                                       _p(stream)), "fd_mh_partials")
+
+
+def fd_mh_merge(parts, G, num_heads, O, stream=None):
+    _check(lib().llmdiy_fd_mh_merge(_p(parts), G, num_heads, _p(O), _p(stream)), "fd_mh_merge")
+
+
+def fd_mh_status(work, L, num_heads):
+    return lib().llmdiy_fd_mh_status(_p(work), L, num_heads)
 
 
 def argmax(out, logits, V, stream=None):

@@ -1,0 +1,118 @@
+"""Multi-head split-KV flash decoding (llmdiy_fd_multihead / _partials / _merge)
+against the CPU oracle per head (orc_attention_q1, orc_fd_partial_mlo) and,
+where oracle/_ref is built, against the reference's own per-head split kernels
+(fd_v5_split_stage1 + fd_opt_stage2) run on the same inputs.
+
+Inputs follow BASELINE configs 1 and 5: q, K, V ~ N(0, 1) fp16 in the engine
+cache layout (row r of head h at r*stride + h*128).  Tolerance: 1e-3 abs on
+the fp16 outputs (north_star attention tolerance)."""
+import numpy as np
+import pytest
+
+import llmdiy_b200 as L
+import refmath
+from gpu_util import dev, host, max_abs, ref_kernels, torch, zeros16
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(rng, L_, H, stride):
+    q = refmath.h(rng.standard_normal(H * 128))
+    K = refmath.h(rng.standard_normal(L_ * stride))
+    V = refmath.h(rng.standard_normal(L_ * stride))
+    return q, K, V
+
+
+def _work(L_, H):
+    t = torch()
+    n = L.fd_mh_work_bytes(L_, H)
+    assert n > 0
+    return t.empty((n + 3) // 4, dtype=t.float32, device="cuda"), n
+
+
+def _multihead(q, K, V, L_, H, stride):
+    dq, dK, dV, O = dev(q), dev(K), dev(V), zeros16(H * 128)
+    w, n = _work(L_, H)
+    L.fd_multihead(dq.data_ptr(), dK.data_ptr(), dV.data_ptr(), O.data_ptr(), L_, stride, H, w.data_ptr(), n)
+    got = host(O).reshape(H, 128)
+    assert L.fd_mh_status(w.data_ptr(), L_, H) == 0
+    return got, (dq, dK, dV)
+
+
+@pytest.mark.parametrize("L_,H,stride", [(1024, 16, 2048), (1, 16, 2048), (63, 16, 2048), (65, 4, 512),
+                                         (1000, 16, 2048), (4097, 2, 256), (32768, 16, 2048)])
+def test_fd_multihead_vs_oracle(oracle, rng, L_, H, stride):
+    q, K, V = _inputs(rng, L_, H, stride)
+    got, _ = _multihead(q, K, V, L_, H, stride)
+    for h in range(H):
+        exp = oracle.attention_q1(q[h * 128:(h + 1) * 128], K[h * 128:], V[h * 128:], L_, stride)
+        assert max_abs(got[h], exp) < 1e-3, h
+
+
+def test_fd_multihead_vs_reference_split(oracle, rng):
+    """Config 1 against the reference's split kernels run head by head."""
+    ref = ref_kernels()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    t = torch()
+    L_, H, stride = 1024, 16, 2048
+    q, K, V = _inputs(rng, L_, H, stride)
+    got, (dq, dK, dV) = _multihead(q, K, V, L_, H, stride)
+    nc = (L_ + 255) // 256
+    for h in range(H):
+        Op = zeros16(nc * 128)
+        lse = t.zeros(nc, dtype=t.float32, device="cuda")
+        r = zeros16(128)
+        off = h * 128 * 2  # bytes
+        ref.fd_v5_split_stage1(dq.data_ptr() + off, dK.data_ptr() + off, dV.data_ptr() + off, Op.data_ptr(),
+                               lse.data_ptr(), L_, nc, stride)
+        ref.fd_opt_stage2(Op.data_ptr(), lse.data_ptr(), r.data_ptr(), nc)
+        assert max_abs(got[h], host(r)) < 1e-3, h
+
+
+@pytest.mark.parametrize("shards", [[5000], [1234, 2000, 1766], [1, 4095], [777, 777, 777, 777]])
+def test_fd_shard_partials_merge(oracle, rng, shards):
+    """Config 5's data path on one GPU: contiguous KV shards -> one partial per head each
+    -> log-sum-exp merge in shard order == attention over the whole cache."""
+    t = torch()
+    H, stride = 16, 2048
+    Lt = sum(shards)
+    q, K, V = _inputs(rng, Lt, H, stride)
+    dq, dK, dV = dev(q), dev(K), dev(V)
+    parts = t.zeros((len(shards), H, 130), dtype=t.float32, device="cuda")
+    r0 = 0
+    for g, n in enumerate(shards):
+        w, nb = _work(n, H)
+        off = r0 * stride * 2
+        L.fd_mh_partials(dq.data_ptr(), dK.data_ptr() + off, dV.data_ptr() + off, n, stride, H,
+                         parts[g].data_ptr(), w.data_ptr(), nb)
+        r0 += n
+    O = zeros16(H * 128)
+    L.fd_mh_merge(parts.data_ptr(), len(shards), H, O.data_ptr())
+    got = host(O).reshape(H, 128)
+    hp = host(parts)
+    r0 = 0
+    for g, n in enumerate(shards):
+        for h in (0, H - 1):
+            m, l, o = oracle.fd_partial_mlo(q[h * 128:(h + 1) * 128], K[r0 * stride + h * 128:],
+                                            V[r0 * stride + h * 128:], n, stride)
+            assert abs(hp[g, h, 128] - m) < 1e-4 * max(1.0, abs(m))
+            assert abs(hp[g, h, 129] - l) < 1e-4 * max(1.0, abs(l))
+            assert max_abs(hp[g, h, :128] / hp[g, h, 129], o / l) < 1e-4
+        r0 += n
+    for h in range(H):
+        exp = oracle.attention_q1(q[h * 128:(h + 1) * 128], K[h * 128:], V[h * 128:], Lt, stride)
+        assert max_abs(got[h], exp) < 1e-3, h
+
+
+def test_fd_multihead_rejects_bad_arguments(rng):
+    t = torch()
+    x = t.zeros(4096, dtype=t.float16, device="cuda")
+    w = t.zeros(1 << 16, dtype=t.float32, device="cuda")
+    p = x.data_ptr()
+    with pytest.raises(L.LlmdiyError):
+        L.fd_multihead(p, p, p, p, 16, 1000, 16, w.data_ptr(), 1 << 18)  # stride < heads * 128
+    with pytest.raises(L.LlmdiyError):
+        L.fd_multihead(p + 2, p, p, p, 16, 2048, 16, w.data_ptr(), 1 << 18)  # misaligned q
+    with pytest.raises(L.LlmdiyError):
+        L.fd_multihead(p, p, p, p, 16, 2048, 16, w.data_ptr(), 4)  # workspace too small
