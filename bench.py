@@ -379,17 +379,18 @@ def run_fd_op(args, rank, world, local, pg):
         torch.cuda.empty_cache()
     # ---- config 5: L = 131072 over the ranks
     Lt = 131072
-    Lr = Lt // world
+    import llmdiy_dist as D
     q = torch.randn(FD_HEADS * 128, generator=g, device=dev).half()
     if pg is not None:
         pg.broadcast(q, src=0)
+    att = D.SplitKVAttention(pg.group.WORLD if pg is not None else None, FD_HEADS, FD_STRIDE)
+    r0, r1 = att.rows(Lt)
+    Lr = r1 - r0
     K = torch.randn(Lr * FD_STRIDE, generator=g, device=dev).half()
     V = torch.randn(Lr * FD_STRIDE, generator=g, device=dev).half()
     O = torch.empty(FD_HEADS * 128, dtype=torch.float16, device=dev)
     nb = L.fd_mh_work_bytes(Lr, FD_HEADS)
     work = torch.empty((nb + 3) // 4, dtype=torch.float32, device=dev)
-    part = torch.empty((FD_HEADS, 130), dtype=torch.float32, device=dev)
-    parts = torch.empty((world, FD_HEADS, 130), dtype=torch.float32, device=dev)
     st = torch.cuda.current_stream(dev)
 
     def call():
@@ -397,10 +398,7 @@ def run_fd_op(args, rank, world, local, pg):
             L.fd_multihead(q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), Lr, FD_STRIDE, FD_HEADS,
                            work.data_ptr(), nb, stream=st.cuda_stream)
         else:
-            L.fd_mh_partials(q.data_ptr(), K.data_ptr(), V.data_ptr(), Lr, FD_STRIDE, FD_HEADS, part.data_ptr(),
-                             work.data_ptr(), nb, stream=st.cuda_stream)
-            pg.all_gather_into_tensor(parts, part)
-            L.fd_mh_merge(parts.data_ptr(), world, FD_HEADS, O.data_ptr(), stream=st.cuda_stream)
+            att(q, K, V, Lt, O)  # partials -> NCCL all-gather -> merge, all on the current stream
 
     for _ in range(max(3, args.warmup)):
         call()
@@ -415,7 +413,8 @@ def run_fd_op(args, rank, world, local, pg):
     barrier(pg, local)
     ms = max_over_ranks(pg, e0.elapsed_time(e1) / reps, local)
     gbs = fd_bytes(Lt) / (ms * 1e-3) / 1e9
-    assert L.fd_mh_status(work.data_ptr(), Lr, FD_HEADS) == 0
+    wk = work if world == 1 else att._work
+    assert L.fd_mh_status(wk.data_ptr(), Lr, FD_HEADS) == 0
     lines.append({"metric": "flash_decode_GBps", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world,
                   "us_per_call": round(ms * 1000, 2), "higher_is_better": True, "scaling": "strong",
                   "dtype": "fp16 (fp32 accumulate)", "data": "synthetic N(0,1)",

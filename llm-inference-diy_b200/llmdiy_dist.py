@@ -1,0 +1,102 @@
+"""Multi-GPU split-KV decode attention (one query token over a very long KV cache).
+
+The cache's positions are sharded contiguously over the ranks of a process group
+(one process per GPU).  Each rank computes one partial per head over its shard
+-- o[128] unnormalised, m (max score), l (sum of e^{s - m}) as 130 fp32 --
+with llmdiy_fd_mh_partials, the partials are all-gathered (NCCL over NVLink on
+GPUs), and every rank merges them in rank order with llmdiy_fd_mh_merge.  This
+is the only exchange on the path: 130 x num_heads fp32 per rank.
+
+The reference has no multi-GPU path; its single-GPU counterpart is the per-head
+split-KV pair fd_v5_split_stage1 + fd_opt_stage2
+(kernels/flash_decode_q1_opt.cuh:548-724), whose log-sum-exp merge this
+generalises from chunks within one GPU to shards across GPUs.
+"""
+from __future__ import annotations
+
+PART = 130  # o[128], m, l
+
+
+def shard_range(L: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [r0, r1) of an L-row cache held by `rank` (contiguous, sizes differ by at most one)."""
+    if L < 0 or world <= 0 or not 0 <= rank < world:
+        raise ValueError("bad shard request")
+    return L * rank // world, L * (rank + 1) // world
+
+
+def gather_partials(group, part, world: int, out=None):
+    """All-gather this rank's [num_heads, 130] partial into [world, num_heads, 130] in rank order."""
+    import torch
+    import torch.distributed as dist
+    if out is None:
+        out = torch.empty((world,) + tuple(part.shape), dtype=part.dtype, device=part.device)
+    if world == 1:
+        out[0].copy_(part)
+        return out
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, part.contiguous(), group=group)
+    else:
+        bufs = list(out.unbind(0))
+        dist.all_gather(bufs, part.contiguous(), group=group)
+    return out
+
+
+class SplitKVAttention:
+    """Distributed decode attention over a sharded cache.
+
+    `partials(q, K, V, rows, part)` and `merge(parts, out)` default to the sm_100a
+    kernels (llmdiy_fd_mh_partials / llmdiy_fd_mh_merge on the current CUDA
+    stream); CPU tests substitute other implementations of the same contracts to
+    exercise the sharding and exchange logic on gloo ranks.
+    """
+
+    def __init__(self, group, num_heads: int, stride: int, partials=None, merge=None):
+        import torch.distributed as dist
+        self.group = group
+        self.world = dist.get_world_size(group) if group is not None else 1
+        self.rank = dist.get_rank(group) if group is not None else 0
+        self.num_heads = num_heads
+        self.stride = stride
+        self._partials = partials or self._gpu_partials
+        self._merge = merge or self._gpu_merge
+        self._work = None
+        self._bufs = None  # (part, parts) reused across calls on one device
+
+    def rows(self, L: int) -> tuple[int, int]:
+        return shard_range(L, self.world, self.rank)
+
+    def __call__(self, q, K_shard, V_shard, L: int, out):
+        """q: [num_heads*128] fp16; K_shard/V_shard: this rank's rows of the cache (row stride
+        `stride`); L: total rows over all ranks; out: [num_heads*128] fp16, the same on every rank."""
+        import torch
+        r0, r1 = self.rows(L)
+        if self._bufs is None or self._bufs[0].device != q.device:
+            self._bufs = (torch.empty((self.num_heads, PART), dtype=torch.float32, device=q.device),
+                          torch.empty((self.world, self.num_heads, PART), dtype=torch.float32, device=q.device))
+        part, parts = self._bufs
+        self._partials(q, K_shard, V_shard, r1 - r0, part)
+        gather_partials(self.group, part, self.world, parts)
+        self._merge(parts, out)
+        return out
+
+    # ---- default implementations: the sm_100a kernels
+    def _gpu_partials(self, q, K, V, rows, part):
+        import torch
+        import llmdiy_b200 as L
+        if rows <= 0:
+            # an empty shard contributes nothing: m = -inf, l = 0, o = 0
+            part.zero_()
+            part[:, 128] = float("-inf")
+            return
+        nb = L.fd_mh_work_bytes(rows, self.num_heads)
+        if self._work is None or self._work.numel() * 4 < nb:
+            self._work = torch.empty((nb + 3) // 4, dtype=torch.float32, device=q.device)
+        st = torch.cuda.current_stream(q.device).cuda_stream
+        L.fd_mh_partials(q.data_ptr(), K.data_ptr(), V.data_ptr(), rows, self.stride, self.num_heads,
+                         part.data_ptr(), self._work.data_ptr(), nb, stream=st)
+
+    def _gpu_merge(self, parts, out):
+        import torch
+        import llmdiy_b200 as L
+        st = torch.cuda.current_stream(parts.device).cuda_stream
+        L.fd_mh_merge(parts.data_ptr(), parts.shape[0], self.num_heads, out.data_ptr(), stream=st)
