@@ -52,6 +52,16 @@ int llmdiy_fd_v5_split_stage1(const uint16_t* Q, const uint16_t* K, const uint16
  * <<<1,128>>> (qwen_infer.cu:674-676). */
 int llmdiy_fd_opt_stage2(const uint16_t* Opart, const float* LSE, uint16_t* O, int num_chunks, void* stream);
 
+/* ---- tensor-core GEMM (new entry point: the reference's prefill GEMM is hgemm_swizzle_nn with the
+ * weights transposed to [K,N] and fp16 accumulation, kernels/hgemm_mma_swizzle.cuh:414).
+ * C[M,N] = A[M,K] * W[N,K]^T with W in the .bin file's [out,in] layout, fp16 operands, fp32
+ * accumulation on the tcgen05 tensor cores (TMEM accumulators, TMA-staged 128x128x64 tiles), fp16 C.
+ * K must be a multiple of 8 and the pointers 16-byte aligned. */
+int llmdiy_gemm_tc(const uint16_t* A, const uint16_t* W, uint16_t* C, int M, int N, int K, void* stream);
+/* After synchronising: 0, or 1 if a tensor-core GEMM on this device had a pipeline wait expire since the
+ * last call (its output is then not valid). */
+int llmdiy_gemm_tc_status(void);
+
 /* ---- multi-head split-KV flash decoding (new entry points: the reference attends one head per
  * launch with fd_v5_split_stage1 + fd_opt_stage2, kernels/flash_decode_q1_opt.cuh:548-724, called per
  * head at qwen_infer.cu:650-677).  Q is [num_heads][128] fp16; K and V are the engine's cache layout,

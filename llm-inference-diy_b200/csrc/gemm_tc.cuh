@@ -1,0 +1,130 @@
+// gemm_tc.cuh — C[M, N] = A[M, K] * B[N, K]^T on the tcgen05 tensor cores
+// (fp16 operands, fp32 accumulation in TMEM), with the output op fused into
+// the epilogue.  Both operands are K-major (row-major A; B = weights in the
+// file's [out, in] layout), staged by 2-D TMA loads with 128-byte swizzling
+// through a STAGES-deep shared-memory ring.
+//
+// One 128 x BN output tile per CTA, 4 warps:
+//   warp 0 lane 0  TMA producer (waits for a stage to be released, loads A, B)
+//   warp 1 lane 0  MMA issuer (4 x 128xBNx16 per 64-wide K block, commit
+//                  releases the stage; a final commit signals the accumulator)
+//   warps 0-3      epilogue: warp w owns accumulator rows 32w..32w+31 (its
+//                  TMEM lanes), reads 16 columns at a time, applies the op.
+// Every wait is bounded; on expiry the CTA records an error, waits (bounded)
+// for its in-flight work, frees its TMEM and returns.
+#pragma once
+#include <cuda.h>
+
+#include "tc.cuh"
+
+namespace llmdiy {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;  // 128 bytes of fp16: one swizzle row
+constexpr int kGemmStages = 4;
+constexpr int kGemmThreads = 128;
+
+template <int BN>
+struct GemmSmem {
+    half a[kGemmStages][kGemmBM * kGemmBK];  // each stage 16 KB, 1024-byte aligned
+    half b[kGemmStages][BN * kGemmBK];
+    uint64_t full[kGemmStages];
+    uint64_t empty[kGemmStages];
+    uint64_t accum;
+    uint32_t tmem_base;
+    int fail;
+};
+
+// The epilogue op receives, per thread, one output row and 16 consecutive
+// columns [n, n+16) of fp32 accumulators (already masked to n < N by the caller
+// only at whole-16 granularity: the op checks its own column bound).
+template <int BN, class Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_k(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, int M, int N, int K,
+              Epi epi, int* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    GemmSmem<BN>& s = *reinterpret_cast<GemmSmem<BN>*>(smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m0 = blockIdx.y * kGemmBM, n0 = blockIdx.x * BN;
+    const int KB = (K + kGemmBK - 1) / kGemmBK;
+    constexpr uint32_t kStageBytes = (kGemmBM + BN) * kGemmBK * 2;
+    constexpr uint32_t kCols = BN < 32 ? 32 : BN;  // TMEM columns: a power of two >= 32
+    if (tid == 0) {
+        for (int i = 0; i < kGemmStages; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.empty[i], 1);
+        }
+        mbar_init(&s.accum, 1);
+        s.fail = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&s.tmem_base, kCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s.tmem_base;
+
+    int issued = 0;  // producer: K blocks whose loads were issued
+    if (warp == 0 && lane == 0) {
+        for (int kb = 0; kb < KB; ++kb) {
+            const int st = kb % kGemmStages;
+            if (kb >= kGemmStages && !mbar_wait(&s.empty[st], ((kb / kGemmStages) - 1) & 1, &s.fail)) {
+                s.fail = 1;
+                break;
+            }
+            mbar_arrive_expect_tx(&s.full[st], kStageBytes);
+            tma_load_2d(s.a[st], &tma, kb * kGemmBK, m0, &s.full[st]);
+            tma_load_2d(s.b[st], &tmb, kb * kGemmBK, n0, &s.full[st]);
+            ++issued;
+        }
+    } else if (warp == 1 && lane == 0) {
+        constexpr uint32_t idesc = umma_idesc_f16_f32(kGemmBM, BN);
+        int kb = 0;
+        for (; kb < KB; ++kb) {
+            const int st = kb % kGemmStages;
+            if (!mbar_wait(&s.full[st], (kb / kGemmStages) & 1, &s.fail)) {
+                s.fail = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(s.a[st]), b0 = smem_u32(s.b[st]);
+#pragma unroll
+            for (int k = 0; k < kGemmBK / 16; ++k)
+                umma_f16(tmem, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc,
+                         (kb | k) != 0 ? 1u : 0u);
+            umma_commit(&s.empty[st]);  // frees the stage once these MMAs have read it
+        }
+        umma_commit(&s.accum);  // all MMAs issued so far (a failed loop commits what it has)
+    }
+    __syncwarp();
+    // epilogue
+    const bool ok = __syncthreads_and(mbar_wait(&s.accum, 0, &s.fail) && !s.fail);  // CTA-uniform
+    tc_fence_after();
+    if (ok) {
+        const int row = m0 + warp * 32 + lane;
+        const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+            if (n0 + c >= N) break;  // warp-uniform
+            uint32_t r[16];
+            tmem_ld16(lane_addr + (uint32_t)c, r);
+            tmem_ld_wait();
+            if (row < M) epi(row, n0 + c, reinterpret_cast<const float*>(r));
+        }
+    } else if (tid == 0) {
+        atomicExch(err, 1);
+    }
+    // the producer's loads that no MMA consumed must land before the CTA exits
+    if (warp == 0 && lane == 0 && !ok) {
+        for (int kb = issued > kGemmStages ? issued - kGemmStages : 0; kb < issued; ++kb)
+            (void)mbar_wait(&s.full[kb % kGemmStages], (kb / kGemmStages) & 1);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, kCols);
+}
+
+}  // namespace llmdiy

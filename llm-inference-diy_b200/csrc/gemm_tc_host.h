@@ -1,0 +1,40 @@
+// gemm_tc_host.h — host-side launcher of the tcgen05 GEMM (C = A * W^T with a
+// fused epilogue op) for every translation unit that instantiates one.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "gemm_tc.cuh"
+
+namespace llmdiy {
+constexpr int kGemmBN = 128;  // output columns per CTA tile
+// K-major fp16 operand [rows][K] (row pitch ld elements), box 64 x box_rows, 128-byte swizzle.
+bool make_kmajor_map(CUtensorMap* m, const void* base, int rows, int K, int ld, int box_rows);
+int* gemm_err_word();  // per-device error word of the GEMM kernels (set when a wait expires)
+int gemm_tc_status();  // 0, or 1 once any GEMM of this device recorded an expired wait
+
+// C tile op `epi` is called per thread with (row, first column, 16 fp32 values).
+template <class Epi>
+int launch_gemm_tc(const half* A, int lda, const half* W, int ldw, int M, int N, int K, const Epi& epi,
+                   cudaStream_t st) {
+    if (M <= 0 || N <= 0 || K <= 0) return (int)cudaErrorInvalidValue;
+    constexpr int BN = kGemmBN;
+    CUtensorMap ta, tb;
+    if (!make_kmajor_map(&ta, A, M, K, lda, kGemmBM) || !make_kmajor_map(&tb, W, N, K, ldw, BN))
+        return (int)cudaErrorInvalidValue;
+    int* err = gemm_err_word();
+    if (!err) return (int)cudaErrorMemoryAllocation;
+    auto kern = gemm_tc_k<BN, Epi>;
+    static std::once_flag attr;
+    std::call_once(attr, [&] {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(GemmSmem<BN>));
+    });
+    dim3 grid((N + BN - 1) / BN, (M + kGemmBM - 1) / kGemmBM);
+    kern<<<grid, kGemmThreads, sizeof(GemmSmem<BN>), st>>>(ta, tb, M, N, K, epi, err);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace llmdiy

@@ -71,6 +71,8 @@ def lib() -> ctypes.CDLL:
         "llmdiy_fd_v5_fused": [P, P, P, P, I, I, P],
         "llmdiy_fd_v5_split_stage1": [P, P, P, P, P, I, I, I, P],
         "llmdiy_fd_opt_stage2": [P, P, P, I, P],
+        "llmdiy_gemm_tc": [P, P, P, I, I, I, P],
+        "llmdiy_gemm_tc_status": [],
         "llmdiy_fd_multihead": [P, P, P, P, I, I, I, P, SZ, P],
         "llmdiy_fd_mh_partials": [P, P, P, I, I, I, P, P, SZ, P],
         "llmdiy_fd_mh_merge": [P, I, I, P, P],
@@ -170,6 +172,15 @@ def fd_v5_split_stage1(Q, K, V, Opart, LSE, L, num_chunks, stride, stream=None):
 
 def fd_opt_stage2(Opart, LSE, O, num_chunks, stream=None):
     _check(lib().llmdiy_fd_opt_stage2(_p(Opart), _p(LSE), _p(O), num_chunks, _p(stream)), "fd_opt_stage2")
+
+
+def gemm_tc(A, W, C, M, N, K, stream=None):
+    """C[M,N] = A[M,K] @ W[N,K]^T on the tcgen05 tensor cores (fp16 in/out, fp32 accumulation)."""
+    _check(lib().llmdiy_gemm_tc(_p(A), _p(W), _p(C), M, N, K, _p(stream)), "gemm_tc")
+
+
+def gemm_tc_status():
+    return lib().llmdiy_gemm_tc_status()
 
 
 def fd_mh_work_bytes(L, num_heads):
