@@ -21,7 +21,9 @@
 #include <vector>
 
 #include "decode.h"
+#include "gemm_tc_host.h"
 #include "llmdiy_engine.h"
+#include "prefill_tc.h"
 #include "qwdf.h"
 
 namespace llmdiy {
@@ -81,6 +83,8 @@ struct llmdiy_engine {
     unsigned long long* ll = nullptr;  // flag-carrying words: qkv | att | xo | act | xc
     size_t ll_words = 0;
     uint32_t tag_base = 0;
+    half* pf = nullptr;  // tensor-core prefill scratch: x, xn, q, att [rows][H], act [rows][IM]
+    int pf_rows = 0;
     uint2* feed_tbl = nullptr;  // decode kernel's per-CTA weight-chunk schedule of one step
     int* feed_cnt = nullptr;
     int feed_stride = 0;
@@ -256,6 +260,8 @@ int alloc_state(llmdiy_engine* e) {
     CK(cudaHostGetDevicePointer(&e->host_tokens_dev, e->host_tokens, 0), "map tokens");
     CK(cudaHostAlloc(&e->host_count, sizeof(int) * 4, cudaHostAllocMapped), "alloc mapped count");
     CK(cudaHostGetDevicePointer(&e->host_count_dev, e->host_count, 0), "map count");
+    e->pf_rows = (int)std::min<uint32_t>(c.max_seqlen, (uint32_t)kPrefillChunk);
+    CK(cudaMalloc(&e->pf, (size_t)e->pf_rows * (4 * H + c.intermediate_size) * 2), "alloc prefill scratch");
     return llmdiy_engine_reset(e);
 }
 
@@ -398,10 +404,27 @@ int prefill_impl(llmdiy_engine* e, const int* tokens, int n) {
     for (int i = 0; i < n; ++i)
         if (tokens[i] < 0 || tokens[i] >= (int)e->cfg.vocab_size) return fail(e, LLMDIY_ERR_ARG, "token id out of range");
     CK(cudaMemcpyAsync(e->forced_dev, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, e->stream), "upload prompt");
-    int rc = launch(e, tokens[0], 0, n, true, false, false, e->stream);
-    if (rc) return rc;
+    const llmdiy_config& c = e->cfg;
+    const size_t H = c.hidden_size, R = (size_t)e->pf_rows;
+    PrefillArgs p{};
+    p.layers = e->layers.data();
+    p.wte = e->wte;
+    p.kc = e->kc;
+    p.vc = e->vc;
+    p.NL = (int)c.num_layers;
+    p.IM = (int)c.intermediate_size;
+    p.max_seqlen = (int)c.max_seqlen;
+    p.x = e->pf;
+    p.xn = p.x + R * H;
+    p.q = p.xn + R * H;
+    p.att = p.q + R * H;
+    p.act = p.att + R * H;
+    p.hidden = e->x;
+    int rc = prefill_tc(p, e->forced_dev, n, 0, e->stream);
+    if (rc) return cuda_fail(e, (cudaError_t)rc, "prefill");
     CK(cudaStreamSynchronize(e->stream), "prefill");
-    return read_status(e, nullptr);
+    if (gemm_tc_status()) return fail(e, LLMDIY_ERR_DEVICE, "prefill GEMM pipeline wait expired");
+    return LLMDIY_OK;
 }
 
 }  // namespace
@@ -463,6 +486,7 @@ void llmdiy_engine_destroy(llmdiy_engine* e) {
     cudaSetDevice(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
     cudaFree(e->wbuf);
+    cudaFree(e->pf);
     cudaFree(e->feed_tbl);
     cudaFree(e->feed_cnt);
     cudaFree(e->d_layers);
