@@ -428,6 +428,58 @@ def run_fd_op(args, rank, world, local, pg):
             print(json.dumps(ln), flush=True)
 
 
+# ------------------------------------------------------------------ prefill (config 3)
+def prefill_flops(N, c=QWEN):
+    """GEMM FLOPs of an N-token prompt forward (no lm_head) plus causal attention (QK^T and PV)."""
+    H, IM, NL = c["hidden_size"], c["intermediate_size"], c["num_layers"]
+    gemm = 2 * N * (3 * H * H + H * H + 2 * IM * H + H * IM) * NL
+    attn = 2 * 2 * H * (N * (N + 1) // 2) * NL
+    return gemm, attn
+
+
+def run_prefill(args, rank, world, local, pg):
+    """Qwen-1.8B prompt forward of 2048 uniform-random ids through the public
+    API (llmdiy_engine_prefill: ids uploaded from host, KV cache filled, synchronised), wall-clock
+    per prefill, TFLOP/s against the measured dense fp16/bf16 tensor peak."""
+    import numpy as np
+    import torch
+    import llmdiy_b200 as L
+    torch.cuda.set_device(local)
+    N = 2048
+    cfg = L.make_config(**QWEN, max_seqlen=N + 64)
+    eng = L.Engine(config=cfg, seed=SEED, device=local)
+    ids = np.random.default_rng(PROMPT_SEED + rank).integers(0, QWEN["vocab_size"], N).tolist()
+    for _ in range(max(1, args.warmup)):
+        eng.prefill(ids)
+    barrier(pg, local)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.prefill(ids)
+    dt = (time.perf_counter() - t0) / args.steps
+    barrier(pg, local)
+    dt = max_over_ranks(pg, dt, local)
+    gemm, attn = prefill_flops(N)
+    tf = (gemm + attn) / dt / 1e12
+    peak = 1665.2
+    mp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(mp):
+        peak = float(json.load(open(mp))["bf16_tflops"])
+    if rank == 0:
+        print(json.dumps({"metric": "prefill_ms", "value": round(dt * 1e3, 3), "unit": "ms", "n_gpus": world,
+                          "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+                          "scaling": "weak", "dtype": "fp16 (fp32 accumulate)",
+                          "data": "synthetic: seeded N(0,0.02) fp16 weights, uniform random prompt ids",
+                          "config": {"workload": "BASELINE configs[2]: Qwen-1.8B prefill of 2048 tokens "
+                                     "(no lm_head; the last prompt token goes through decode)",
+                                     "timing": "wall clock around llmdiy_engine_prefill (host ids in, synchronised)"},
+                          "tflops": round(tf, 1), "gemm_tflop": round(gemm / 1e12, 3),
+                          "attention_tflop": round(attn / 1e12, 3),
+                          "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak,
+                                       "unit": "TFLOP/s", "frac": round(tf / peak, 4), "peak_kind": "measured"}}),
+              flush=True)
+    eng.close()
+
+
 def run_ncu_case():
     """Small case for ncu captures of decode_kernel: the Qwen-1.8B shapes with 4 layers (full vocab,
     0.95 GB of weights, larger than L2), one prefill launch of 127 tokens, then one decode launch of
@@ -457,15 +509,23 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", action="store_true", help="run the small decode case used for ncu captures")
-    ap.add_argument("--workload", default="decode", choices=["decode", "fd-op"],
-                    help="decode: the headline config-2 line; fd-op: flash-decoding op lines (configs 1 and 5)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "fd-op", "prefill"],
+                    help="decode: the headline config-2 line; fd-op: flash-decoding op lines (configs 1 and 5); "
+                         "prefill: 2048-token prompt forward (config 3)")
     args = ap.parse_args()
     if args.ncu_case:
         run_ncu_case()
         return
     rank, world, local, pg = dist_setup(args.gpus)
     try:
-        if args.workload == "fd-op":
+        if args.workload == "prefill":
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "workload": "prefill", "unavailable":
+                                      "the reference has no CPU prefill path; see the decode arm"}))
+            else:
+                run_prefill(args, rank, world, local, pg)
+        elif args.workload == "fd-op":
             if args.impl == "reference":
                 if rank == 0:
                     print(json.dumps({"impl": "reference", "workload": "fd-op", "unavailable":

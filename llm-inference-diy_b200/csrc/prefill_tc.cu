@@ -1,7 +1,8 @@
 // prefill_tc.cu — the prompt forward (QwenEngine::prefill, qwen_infer.cu:372-611)
 // on the tensor cores: per layer
 //   RMSNorm(ln_1) rows -> QKV GEMM [epilogue: bias, RoPE, K/V appended to the
-//   cache, Q kept] -> causal attention over the cache -> o_proj GEMM [epilogue:
+//   cache, Q kept] -> causal flash attention over the cache (flash_prefill.cuh)
+//   -> o_proj GEMM [epilogue:
 //   residual add] -> RMSNorm(ln_2) rows -> w1|w2 GEMM [epilogue: SwiGLU] ->
 //   c_proj GEMM [epilogue: residual add].
 // The GEMMs are the tcgen05 kernel (gemm_tc.cuh) over the engine's device
@@ -11,7 +12,10 @@
 // epilogues, so a prompt row gets the same arithmetic as a decode step except
 // for the GEMM summation order.  Prompts are processed in chunks of at most
 // kPrefillChunk rows; a chunk attends over every cached row before it.
+#include <mutex>
+
 #include "decode.h"
+#include "flash_prefill.cuh"
 #include "gemm_tc_host.h"
 #include "ops.cuh"
 #include "prefill_tc.h"
@@ -41,32 +45,6 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_k(half* __restrict__ out, co
     *reinterpret_cast<uint4*>(out + (size_t)r * kHidden + 8 * t) = pack8(of);
 }
 
-// Causal attention of query rows at positions p0 .. p0+n-1 over the cache:
-// one warp per (row, head), rows [0, pos] of the head (attend_rows, the same
-// online softmax as the decode path), scale __frcp_rn(sqrt(128)).
-__global__ void __launch_bounds__(256) prefill_attn_k(const half* __restrict__ q, const half* __restrict__ kc,
-                                                      const half* __restrict__ vc, half* __restrict__ att, int n,
-                                                      int p0) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, dl = (lane & 15) * 8;
-    const int i = blockIdx.x * 8 + warp, h = blockIdx.y;
-    if (i >= n) return;
-    float q8[8];
-    unpack8(*reinterpret_cast<const uint4*>(q + (size_t)i * kHidden + h * kHeadDim + dl), q8);
-    const float scale = __frcp_rn(sqrtf((float)kHeadDim));
-    float m = -INFINITY, l = 0.f, o8[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) o8[e] = 0.f;
-    attend_rows<true>(kc + h * kHeadDim, vc + h * kHeadDim, kHidden, 0, p0 + i + 1, q8, scale, m, l, o8);
-    combine_halfwarps(m, l, o8);
-    if (lane < 16) {
-        const float inv = __frcp_rn(l);
-        float of[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) of[e] = o8[e] * inv;
-        *reinterpret_cast<uint4*>(att + (size_t)i * kHidden + h * kHeadDim + dl) = pack8(of);
-    }
-}
-
 // QKV epilogue: columns (2u, 2u+1) are RoPE partners (t, t+64) of unit u =
 // sec*1024 + h*64 + t.  bias -> RoPE (q, k) -> q kept in [row][H], k and v
 // appended to the cache at position p0 + row (fused_qkv_rope_cache.cuh:6-55).
@@ -76,27 +54,39 @@ struct EpiQKV {
     half* kc;
     half* vc;
     int p0;
+    // The 16 columns [n, n+16) are units u0..u0+7 = dims t0..t0+7 (and +64) of one
+    // head of one section (n is a multiple of 16), so the 8 first values and the 8
+    // second values of the pairs are each one 16-byte row segment.
     __device__ void operator()(int row, int n, const float* v) const {
         const int pos = p0 + row;
+        const int u0 = n >> 1, sec = u0 / (kHidden / 2), vv = u0 % (kHidden / 2), h = vv / 64, t0 = vv % 64;
+        const int i1 = sec * kHidden + h * kHeadDim + t0;
+        float b1[8], b2[8], y1[8], y2[8];
+        unpack8(*reinterpret_cast<const uint4*>(bias + i1), b1);
+        unpack8(*reinterpret_cast<const uint4*>(bias + i1 + 64), b2);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int u = (n >> 1) + j, sec = u / (kHidden / 2), vv = u % (kHidden / 2), h = vv / 64, t = vv % 64;
-            const int i1 = sec * kHidden + h * kHeadDim + t;
-            const float y1 = h2f(f2h(h2f(f2h(v[2 * j])) + h2f(bias[i1])));
-            const float y2 = h2f(f2h(h2f(f2h(v[2 * j + 1])) + h2f(bias[i1 + 64])));
-            const int o1 = h * kHeadDim + t, o2 = o1 + 64;
-            if (sec == 2) {
-                vc[(size_t)pos * kHidden + o1] = f2h(y1);
-                vc[(size_t)pos * kHidden + o2] = f2h(y2);
-            } else {
-                const float theta = (float)pos * __powf(10000.0f, __fdividef(-2.0f * (float)t, (float)kHeadDim));
-                const float cs = __cosf(theta), sn = __sinf(theta);
-                const half r1 = f2h(y1 * cs - y2 * sn), r2 = f2h(y2 * cs + y1 * sn);
-                half* dst = sec == 1 ? kc + (size_t)pos * kHidden : q + (size_t)row * kHidden;
-                dst[o1] = r1;
-                dst[o2] = r2;
-            }
+            y1[j] = h2f(f2h(h2f(f2h(v[2 * j])) + b1[j]));
+            y2[j] = h2f(f2h(h2f(f2h(v[2 * j + 1])) + b2[j]));
         }
+        const int o1 = h * kHeadDim + t0;
+        if (sec == 2) {
+            *reinterpret_cast<uint4*>(vc + (size_t)pos * kHidden + o1) = pack8(y1);
+            *reinterpret_cast<uint4*>(vc + (size_t)pos * kHidden + o1 + 64) = pack8(y2);
+            return;
+        }
+        float r1[8], r2[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float theta =
+                (float)pos * __powf(10000.0f, __fdividef(-2.0f * (float)(t0 + j), (float)kHeadDim));
+            const float cs = __cosf(theta), sn = __sinf(theta);
+            r1[j] = y1[j] * cs - y2[j] * sn;
+            r2[j] = y2[j] * cs + y1[j] * sn;
+        }
+        half* dst = sec == 1 ? kc + (size_t)pos * kHidden : q + (size_t)row * kHidden;
+        *reinterpret_cast<uint4*>(dst + o1) = pack8(r1);
+        *reinterpret_cast<uint4*>(dst + o1 + 64) = pack8(r2);
     }
 };
 
@@ -143,6 +133,11 @@ struct EpiSwiGLU {
 int prefill_tc(const PrefillArgs& p, const int* tokens_dev, int n, int p0, cudaStream_t st) {
     int rc = 0;
     cudaError_t e;
+    static std::once_flag attr;
+    std::call_once(attr, [] {
+        cudaFuncSetAttribute(flash_prefill_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(FlashPrefillSmem));
+    });
     for (int c0 = 0; c0 < n; c0 += kPrefillChunk) {
         const int m = n - c0 < kPrefillChunk ? n - c0 : kPrefillChunk;
         const int pos0 = p0 + c0;
@@ -155,7 +150,8 @@ int prefill_tc(const PrefillArgs& p, const int* tokens_dev, int n, int p0, cudaS
             rc = launch_gemm_tc(p.xn, kHidden, L.qkv_w, kHidden, m, 3 * kHidden, kHidden,
                                 EpiQKV{L.qkv_b, p.q, kcl, vcl, pos0}, st);
             if (rc) return rc;
-            prefill_attn_k<<<dim3((m + 7) / 8, kHeads), 256, 0, st>>>(p.q, kcl, vcl, p.att, m, pos0);
+            flash_prefill_k<<<dim3((m + kFpRows - 1) / kFpRows, kHeads), kFpThreads, sizeof(FlashPrefillSmem), st>>>(
+                p.q, kcl, vcl, p.att, m, pos0, kHidden, kHidden);
             rc = launch_gemm_tc(p.att, kHidden, L.proj_w, kHidden, m, kHidden, kHidden, EpiResidual{p.x}, st);
             if (rc) return rc;
             rmsnorm_rows_k<<<m, 256, 0, st>>>(p.xn, p.x, L.ln2);

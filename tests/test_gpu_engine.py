@@ -92,6 +92,22 @@ def test_prefill_matches_oracle(engine, omodel):
         assert float(np.max(np.abs(v.astype(np.float32) - ov.astype(np.float32)))) < 2e-2
 
 
+def test_long_prefill_matches_oracle(engine, omodel):
+    """A prompt spanning several 64-row query tiles and key tiles of the prefill's flash attention
+    and several 128-row GEMM tiles: the KV rows of the last layer (which depend on every earlier
+    layer's attention) against the oracle's prefill."""
+    rng = np.random.default_rng(15)
+    prompt = rng.integers(0, SMALL["vocab_size"], 333).tolist()
+    engine.reset()
+    omodel.reset()
+    engine.prefill(prompt)
+    omodel.prefill(prompt)
+    k, v = engine.kv(1, 0, 333)
+    ok_, ov = omodel.kv(1, 0, 333)
+    assert float(np.max(np.abs(k.astype(np.float32) - ok_.astype(np.float32)))) < 2e-2
+    assert float(np.max(np.abs(v.astype(np.float32) - ov.astype(np.float32)))) < 2e-2
+
+
 def test_generate_stream_matches_oracle(engine, omodel):
     rng = np.random.default_rng(6)
     prompt = rng.integers(0, SMALL["vocab_size"], 64).tolist()
