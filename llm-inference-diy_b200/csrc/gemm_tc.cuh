@@ -4,7 +4,7 @@
 // file's [out, in] layout), staged by 2-D TMA loads with 128-byte swizzling
 // through a STAGES-deep shared-memory ring.
 //
-// One 128 x BN output tile per CTA, 4 warps:
+// One 128 x BN output tile per CTA (BN = 256: one 128x256x16 MMA per K step of 16), 4 warps:
 //   warp 0 lane 0  TMA producer (waits for a stage to be released, loads A, B)
 //   warp 1 lane 0  MMA issuer (4 x 128xBNx16 per 64-wide K block, commit
 //                  releases the stage; a final commit signals the accumulator)

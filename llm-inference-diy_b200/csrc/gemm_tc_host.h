@@ -10,7 +10,7 @@
 #include "gemm_tc.cuh"
 
 namespace llmdiy {
-constexpr int kGemmBN = 128;  // output columns per CTA tile
+constexpr int kGemmBN = 256;  // output columns per CTA tile (UMMA N = 256)
 // K-major fp16 operand [rows][K] (row pitch ld elements), box 64 x box_rows, 128-byte swizzle.
 bool make_kmajor_map(CUtensorMap* m, const void* base, int rows, int K, int ld, int box_rows);
 int* gemm_err_word();  // per-device error word of the GEMM kernels (set when a wait expires)
