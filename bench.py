@@ -480,6 +480,53 @@ def run_prefill(args, rank, world, local, pg):
     eng.close()
 
 
+# ------------------------------------------------------------------ tensor-core GEMM shapes of configs 3/4
+def run_gemm(args, rank, world, local, pg):
+    """llmdiy_gemm_tc (tcgen05, fp16 in, fp32 accumulate) on the prefill's GEMM shapes, CUDA events,
+    against the measured dense fp16/bf16 peak; cuBLAS (torch.matmul) on the same shapes for context."""
+    import torch
+    import llmdiy_b200 as L
+    torch.cuda.set_device(local)
+    peak = 1665.2
+    mp = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(mp):
+        peak = float(json.load(open(mp))["bf16_tflops"])
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    for (M, N, K) in [(2048, 6144, 2048), (2048, 2048, 2048), (2048, 11008, 2048), (2048, 2048, 5504),
+                      (8192, 8192, 8192)]:
+        A = (torch.randn(M, K, generator=g, device="cuda") * 0.5).half()
+        W = (torch.randn(N, K, generator=g, device="cuda") / K ** 0.5).half()
+        C = torch.empty(M, N, device="cuda", dtype=torch.half)
+        st = torch.cuda.current_stream().cuda_stream
+
+        def ours():
+            L.gemm_tc(A.data_ptr(), W.data_ptr(), C.data_ptr(), M, N, K, stream=st)
+
+        def timed(fn, n=20):
+            for _ in range(max(3, args.warmup)):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(n):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / n
+
+        ms = timed(ours)
+        ms_cublas = timed(lambda: torch.matmul(A, W.t()))
+        tf = 2 * M * N * K / ms / 1e9
+        if rank == 0:
+            print(json.dumps({"metric": "gemm_tflops", "value": round(tf, 1), "unit": "TFLOP/s",
+                              "config": {"workload": f"C[{M},{N}] = A[{M},{K}] W[{N},{K}]^T fp16, fp32 accumulate"},
+                              "us": round(ms * 1e3, 1), "cublas_tflops": round(2 * M * N * K / ms_cublas / 1e9, 1),
+                              "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak,
+                                           "unit": "TFLOP/s", "frac": round(tf / peak, 4), "peak_kind": "measured"}}),
+                  flush=True)
+
+
 def run_ncu_case():
     """Small case for ncu captures of decode_kernel: the Qwen-1.8B shapes with 4 layers (full vocab,
     0.95 GB of weights, larger than L2), one prefill launch of 127 tokens, then one decode launch of
@@ -509,7 +556,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", action="store_true", help="run the small decode case used for ncu captures")
-    ap.add_argument("--workload", default="decode", choices=["decode", "fd-op", "prefill"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "fd-op", "prefill", "gemm"],
                     help="decode: the headline config-2 line; fd-op: flash-decoding op lines (configs 1 and 5); "
                          "prefill: 2048-token prompt forward (config 3)")
     args = ap.parse_args()
@@ -518,7 +565,14 @@ def main():
         return
     rank, world, local, pg = dist_setup(args.gpus)
     try:
-        if args.workload == "prefill":
+        if args.workload == "gemm":
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "workload": "gemm", "unavailable":
+                                      "the reference has no CPU GEMM path; see the decode arm"}))
+            else:
+                run_gemm(args, rank, world, local, pg)
+        elif args.workload == "prefill":
             if args.impl == "reference":
                 if rank == 0:
                     print(json.dumps({"impl": "reference", "workload": "prefill", "unavailable":

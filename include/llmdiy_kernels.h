@@ -55,7 +55,7 @@ int llmdiy_fd_opt_stage2(const uint16_t* Opart, const float* LSE, uint16_t* O, i
 /* ---- tensor-core GEMM (new entry point: the reference's prefill GEMM is hgemm_swizzle_nn with the
  * weights transposed to [K,N] and fp16 accumulation, kernels/hgemm_mma_swizzle.cuh:414).
  * C[M,N] = A[M,K] * W[N,K]^T with W in the .bin file's [out,in] layout, fp16 operands, fp32
- * accumulation on the tcgen05 tensor cores (TMEM accumulators, TMA-staged 128x128x64 tiles), fp16 C.
+ * accumulation on the tcgen05 tensor cores (TMEM accumulators, TMA-staged 128x256x64 tiles), fp16 C.
  * K must be a multiple of 8 and the pointers 16-byte aligned. */
 int llmdiy_gemm_tc(const uint16_t* A, const uint16_t* W, uint16_t* C, int M, int N, int K, void* stream);
 /* After synchronising: 0, or 1 if a tensor-core GEMM on this device had a pipeline wait expire since the
