@@ -480,6 +480,60 @@ def run_prefill(args, rank, world, local, pg):
     eng.close()
 
 
+# ------------------------------------------------------------------ batched ragged decode (config 4)
+def run_batch(args, rank, world, local, pg):
+    """64 independent sequences with KV lengths uniform in [128, 4096] (seeded),
+    their caches pre-filled with N(0,1) fp16, 128 greedy steps each; the sequences are partitioned
+    over the ranks' per-GPU weight replicas with no collective (total work fixed: "strong").
+    Timed on the device per rank (CUDA events around llmdiy_batch_decode, which uploads the start
+    tokens/positions and reads the generated ids back), max over ranks."""
+    import numpy as np
+    import torch
+    import llmdiy_b200 as L
+    torch.cuda.set_device(local)
+    NSEQ, STEPS, LO, HI = 64, 128, 128, 4096
+    rng = np.random.default_rng(17)
+    lens_all = rng.integers(LO, HI + 1, NSEQ)
+    toks_all = rng.integers(0, QWEN["vocab_size"], NSEQ)
+    mine = [i for i in range(NSEQ) if i % world == rank]
+    B = len(mine)
+    cfg = L.make_config(**QWEN, max_seqlen=256)
+    eng = L.Engine(config=cfg, seed=SEED, device=local)
+    bt = L.Batch(eng, max_batch=B, max_len=HI + STEPS + 1)
+    for j, i in enumerate(mine):
+        bt.fill_random(j, int(lens_all[i]), seed=1000 + i)
+    toks = [int(toks_all[i]) for i in mine]
+    pos = [int(lens_all[i]) for i in mine]
+    bt.decode(toks, pos, max(1, args.warmup))  # captures the step
+    barrier(pg, local)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    out = bt.decode(toks, pos, STEPS, stream=st.cuda_stream)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(pg, e0.elapsed_time(e1), local)
+    assert out.shape == (STEPS, B) and (out >= 0).all()
+    value = NSEQ * STEPS / (ms / 1e3)
+    kv_bytes = sum(2 * 2 * 2048 * 24 * (int(lens_all[i]) + s + 1) for i in range(NSEQ) for s in range(STEPS))
+    w_bytes = weight_bytes() * STEPS * world
+    peak, peak_kind = measured_peaks()
+    gbs = (kv_bytes + w_bytes) / (ms / 1e3) / 1e9
+    if rank == 0:
+        print(json.dumps({"metric": "batched_decode_tokens_per_s", "value": round(value, 1), "unit": "tok/s",
+                          "n_gpus": world, "steps": STEPS, "higher_is_better": True, "scaling": "strong",
+                          "ms_per_step": round(ms / STEPS, 3), "dtype": "fp16 (fp32 accumulate)",
+                          "data": "synthetic: seeded N(0,0.02) weights; caches pre-filled N(0,1)",
+                          "config": {"workload": "BASELINE configs[3]: 64 sequences, KV lengths U[128,4096], "
+                                     "128 greedy steps", "sequences_per_gpu": B, "parallelism": f"replicas x{world}"},
+                          "roofline": {"bound": "hbm", "achieved_per_gpu": round(gbs / world, 1), "peak": peak,
+                                       "unit": "GB/s", "frac": round(gbs / world / peak, 4),
+                                       "peak_kind": peak_kind,
+                                       "algorithmic_bytes": kv_bytes + w_bytes}}), flush=True)
+    bt.close()
+    eng.close()
+
+
 # ------------------------------------------------------------------ tensor-core GEMM shapes of configs 3/4
 def run_gemm(args, rank, world, local, pg):
     """llmdiy_gemm_tc (tcgen05, fp16 in, fp32 accumulate) on the prefill's GEMM shapes, CUDA events,
@@ -556,7 +610,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", action="store_true", help="run the small decode case used for ncu captures")
-    ap.add_argument("--workload", default="decode", choices=["decode", "fd-op", "prefill", "gemm"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "fd-op", "prefill", "gemm", "batch"],
                     help="decode: the headline config-2 line; fd-op: flash-decoding op lines (configs 1 and 5); "
                          "prefill: 2048-token prompt forward (config 3)")
     args = ap.parse_args()
@@ -565,7 +619,14 @@ def main():
         return
     rank, world, local, pg = dist_setup(args.gpus)
     try:
-        if args.workload == "gemm":
+        if args.workload == "batch":
+            if args.impl == "reference":
+                if rank == 0:
+                    print(json.dumps({"impl": "reference", "workload": "batch", "unavailable":
+                                      "the reference has no batched path; see the decode arm"}))
+            else:
+                run_batch(args, rank, world, local, pg)
+        elif args.workload == "gemm":
             if args.impl == "reference":
                 if rank == 0:
                     print(json.dumps({"impl": "reference", "workload": "gemm", "unavailable":

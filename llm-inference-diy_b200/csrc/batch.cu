@@ -1,0 +1,708 @@
+// batch.cu — batched greedy decode of independent sequences on one engine's
+// weights (64 sequences with ragged KV lengths).  The
+// reference has no batching; it would run the sequences one after another
+// through QwenEngine::step (qwen_infer.cu:614-737), whose arithmetic each row
+// here follows.
+//
+// One step for B sequences (token[b] at position pos[b] -> next[b]):
+//   embed rows -> per layer { RMSNorm rows -> QKV GEMM (M = B) [bias, RoPE,
+//   K/V appended at each row's own position in its own cache] -> ragged
+//   split-KV attention over each sequence's rows [0, pos[b]] -> o_proj GEMM
+//   [residual] -> RMSNorm rows -> w1|w2 GEMM [SwiGLU] -> c_proj GEMM
+//   [residual] } -> RMSNorm(ln_f) rows -> lm_head GEMM -> per-row ArgMax
+//   (reference tie rule) -> tokens and positions advance on the device.
+// GEMMs are the tcgen05 kernel; with M = B <= 64 rows a GEMM has few output
+// tiles, so the K dimension is split over grid.z until the tiles x slices
+// fill the SMs, and a reduce kernel sums the fp32 slices in order and applies
+// the epilogue op (deterministic).  A step is captured once in a CUDA graph;
+// llmdiy_batch_decode replays it per step.
+//
+// Cache layout per layer: [max_batch][max_len][H] fp16 (row r of sequence b of
+// layer l at ((l * max_batch + b) * max_len + r) * H), the engine's row format.
+#include <cuda.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "engine_internal.h"
+#include "gemm_tc_host.h"
+#include "llmdiy_batch.h"
+#include "llmdiy_engine.h"
+#include "prefill_tc.h"
+#include "rows.cuh"
+
+using namespace llmdiy;
+
+namespace {
+
+constexpr int kBatchMax = 64;
+constexpr int kBRows = 64;   // KV rows per TMA tile
+constexpr int kBSplitRows = 512;  // KV rows per attention work item
+constexpr int kBStages = 6;
+constexpr int kBPart = kHeadDim + 2;
+
+// ---------------------------------------------------------------- GEMM epilogues
+// fp32 partial sums of split-K slice blockIdx.z: ws[(z * M + row) * N + n ..]
+struct EpiPartial {
+    float* ws;
+    int M, N;
+    __device__ void operator()(int row, int n, const float* v) const {
+        float* d = ws + ((size_t)blockIdx.z * M + row) * N + n;
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(d + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    }
+};
+
+// QKV of B sequences: as the prefill's QKV epilogue, with each row's own position and cache.
+struct EpiQKVRows {
+    const half* bias;
+    half* q;          // [B][H]
+    half* kc;         // layer base of the K cache [max_batch][max_len][H]
+    half* vc;
+    const int* pos;   // [B]
+    int max_len;
+    __device__ void operator()(int row, int n, const float* v) const {
+        const int p = pos[row];
+        const int u0 = n >> 1, sec = u0 / (kHidden / 2), vv = u0 % (kHidden / 2), h = vv / 64, t0 = vv % 64;
+        const int i1 = sec * kHidden + h * kHeadDim + t0;
+        float b1[8], b2[8], y1[8], y2[8];
+        unpack8(*reinterpret_cast<const uint4*>(bias + i1), b1);
+        unpack8(*reinterpret_cast<const uint4*>(bias + i1 + 64), b2);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            y1[j] = h2f(f2h(h2f(f2h(v[2 * j])) + b1[j]));
+            y2[j] = h2f(f2h(h2f(f2h(v[2 * j + 1])) + b2[j]));
+        }
+        const int o1 = h * kHeadDim + t0;
+        const size_t crow = ((size_t)row * max_len + p) * kHidden;
+        if (sec == 2) {
+            *reinterpret_cast<uint4*>(vc + crow + o1) = pack8(y1);
+            *reinterpret_cast<uint4*>(vc + crow + o1 + 64) = pack8(y2);
+            return;
+        }
+        float r1[8], r2[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float theta = (float)p * __powf(10000.0f, __fdividef(-2.0f * (float)(t0 + j), (float)kHeadDim));
+            const float cs = __cosf(theta), sn = __sinf(theta);
+            r1[j] = y1[j] * cs - y2[j] * sn;
+            r2[j] = y2[j] * cs + y1[j] * sn;
+        }
+        half* dst = sec == 1 ? kc + crow : q + (size_t)row * kHidden;
+        *reinterpret_cast<uint4*>(dst + o1) = pack8(r1);
+        *reinterpret_cast<uint4*>(dst + o1 + 64) = pack8(r2);
+    }
+};
+
+struct EpiStoreRows {
+    half* C;
+    int N;
+    __device__ void operator()(int row, int n, const float* v) const {
+        half* d = C + (size_t)row * N + n;
+        *reinterpret_cast<uint4*>(d) = pack8(v);
+        *reinterpret_cast<uint4*>(d + 8) = pack8(v + 8);
+    }
+};
+
+// Sum the split-K slices of one (row, 16 columns) in slice order and apply `epi`.
+template <class Epi>
+__global__ void __launch_bounds__(256) splitk_reduce_k(const float* __restrict__ ws, int Z, int M, int N, Epi epi) {
+    const int groups = N / 16;
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= M * groups) return;
+    const int row = idx / groups, n = (idx % groups) * 16;
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+    for (int z = 0; z < Z; ++z) {
+        const float* p = ws + ((size_t)z * M + row) * N + n;
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(p + j);
+            acc[j] += f.x;
+            acc[j + 1] += f.y;
+            acc[j + 2] += f.z;
+            acc[j + 3] += f.w;
+        }
+    }
+    epi(row, n, acc);
+}
+
+// ---------------------------------------------------------------- ragged split-KV attention
+struct BFdSmem {
+    half k[kBStages][kBRows * kHeadDim];
+    half v[kBStages][kBRows * kHeadDim];
+    uint64_t full[kBStages];
+    float so[4][kHeadDim];
+    float sm[4], sl[4];
+    int pre[kBatchMax + 1];  // prefix sums of the items per sequence
+    int nsp[kBatchMax];      // splits per sequence
+};
+
+struct BItem {
+    int b, h, sp, r0, r1;  // sequence, head, split, rows [r0, r1)
+    int tile, ntiles;
+};
+
+__device__ __forceinline__ void bfd_item(const BFdSmem& s, int item, int B, const int* pos, BItem& it) {
+    int b = 0;
+    while (b + 1 < B && s.pre[b + 1] <= item) ++b;
+    const int r = item - s.pre[b], S = s.nsp[b];
+    it.b = b;
+    it.h = r / S;
+    it.sp = r % S;
+    it.r0 = it.sp * kBSplitRows;
+    it.r1 = min(pos[b] + 1, it.r0 + kBSplitRows);
+    it.tile = 0;
+    it.ntiles = (it.r1 - it.r0 + kBRows - 1) / kBRows;
+}
+
+// Items (sequence b, head h, split sp) over a persistent grid; each writes the
+// unnormalised partial (o[128], m, l) of its rows to part[((b*16 + h) * Smax + sp) * 130].
+__global__ void __launch_bounds__(128, 1)
+    bfd_partials_k(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                   const half* __restrict__ q, const int* __restrict__ pos, int B, int max_len, int Smax,
+                   float* __restrict__ part, int* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    BFdSmem& s = *reinterpret_cast<BFdSmem*>(smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hw = lane >> 4, dl = (lane & 15) * 8;
+    const uint64_t pol = l2_policy_evict_first();
+    if (tid == 0) {
+        for (int i = 0; i < kBStages; ++i) mbar_init(&s.full[i], 1);
+        mbar_fence_init();
+        int acc = 0;
+        for (int b = 0; b < B; ++b) {
+            const int S = (pos[b] + 1 + kBSplitRows - 1) / kBSplitRows;
+            s.nsp[b] = S;
+            s.pre[b] = acc;
+            acc += S * kHeads;
+        }
+        s.pre[B] = acc;
+    }
+    __syncthreads();
+    const int nitems = s.pre[B], G = gridDim.x;
+    BItem pc;
+    uint32_t issued = 0, consumed = 0;
+    if (tid == 0 && (int)blockIdx.x < nitems) bfd_item(s, blockIdx.x, B, pos, pc);
+    else pc.b = -1;
+    auto produce = [&]() {
+        if (pc.b < 0) return;
+        while (pc.tile >= pc.ntiles) {
+            const int nxt = (int)(s.pre[pc.b] + pc.h * s.nsp[pc.b] + pc.sp) + G;  // this item's index + G
+            if (nxt >= nitems) { pc.b = -1; return; }
+            bfd_item(s, nxt, B, pos, pc);
+        }
+        const int st = issued % kBStages;
+        const int y = pc.b * max_len + pc.r0 + pc.tile * kBRows;
+        mbar_arrive_expect_tx(&s.full[st], 2 * kBRows * kHeadDim * 2);
+        tma_load_2d_hint(s.k[st], &tk, pc.h * kHeadDim, y, &s.full[st], pol);
+        tma_load_2d_hint(s.v[st], &tv, pc.h * kHeadDim, y, &s.full[st], pol);
+        ++pc.tile;
+        ++issued;
+    };
+    if (tid == 0)
+        for (int i = 0; i < kBStages; ++i) produce();
+    const float scale = __frcp_rn(sqrtf((float)kHeadDim));
+    bool failed = false;
+    for (int item = blockIdx.x; item < nitems && !failed; item += G) {
+        BItem it;
+        bfd_item(s, item, B, pos, it);
+        float q8[8];
+        unpack8(*reinterpret_cast<const uint4*>(q + (size_t)it.b * kHidden + it.h * kHeadDim + dl), q8);
+        float m = -INFINITY, l = 0.f, o8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o8[e] = 0.f;
+        for (int t = 0; t < it.ntiles; ++t, ++consumed) {
+            const int st = consumed % kBStages;
+            const bool ok = mbar_wait(&s.full[st], (consumed / kBStages) & 1);
+            if (__syncthreads_or(!ok)) {
+                failed = true;
+                break;
+            }
+            const int nvalid = min(kBRows, it.r1 - (it.r0 + t * kBRows));
+            const half* kt = s.k[st];
+            const half* vt = s.v[st];
+            float sc[8];
+            uint4 vr[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int r = warp * 16 + 2 * j + hw;
+                float kf[8];
+                unpack8(*reinterpret_cast<const uint4*>(kt + r * kHeadDim + dl), kf);
+                vr[j] = *reinterpret_cast<const uint4*>(vt + r * kHeadDim + dl);
+                float d = 0.f;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) d = __fmaf_rn(q8[e], kf[e], d);
+                sc[j] = d;
+            }
+#pragma unroll
+            for (int mk = 8; mk >= 1; mk >>= 1)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], mk);
+            float mx = m;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                sc[j] = (warp * 16 + 2 * j + hw < nvalid) ? sc[j] * scale : -INFINITY;
+                mx = fmaxf(mx, sc[j]);
+            }
+            if (mx != -INFINITY) {
+                const float corr = __expf(m - mx);
+                l *= corr;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) o8[e] *= corr;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float p = __expf(sc[j] - mx);
+                    l += p;
+                    float vf[8];
+                    unpack8(vr[j], vf);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o8[e] = __fmaf_rn(p, vf[e], o8[e]);
+                }
+                m = mx;
+            }
+            __syncthreads();
+            if (tid == 0) produce();
+        }
+        if (failed) break;
+        combine_halfwarps(m, l, o8);
+        if (lane < 16) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s.so[warp][dl + e] = o8[e];
+        }
+        if (lane == 0) { s.sm[warp] = m; s.sl[warp] = l; }
+        __syncthreads();
+        const int d = tid;
+        float M = -INFINITY;
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, s.sm[w]);
+        float Ls = 0.f, acc = 0.f;
+        for (int w = 0; w < 4; ++w) {
+            if (s.sm[w] == -INFINITY) continue;
+            const float f = __expf(s.sm[w] - M);
+            Ls += s.sl[w] * f;
+            acc = __fmaf_rn(f, s.so[w][d], acc);
+        }
+        float* p = part + ((size_t)(it.b * kHeads + it.h) * Smax + it.sp) * kBPart;
+        p[d] = acc;
+        if (d == 0) { p[kHeadDim] = M; p[kHeadDim + 1] = Ls; }
+        __syncthreads();
+    }
+    if (failed && tid == 0) {
+        atomicExch(err, 1);
+        for (uint32_t i = consumed; i < issued; ++i) (void)mbar_wait(&s.full[i % kBStages], (i / kBStages) & 1);
+    }
+}
+
+// Merge of sequence b, head h: its splits in order -> att[b][h*128 + d] (fp16).
+__global__ void __launch_bounds__(kHeadDim) bfd_merge_k(const float* __restrict__ part, const int* __restrict__ pos,
+                                                        int Smax, half* __restrict__ att) {
+    const int b = blockIdx.x / kHeads, h = blockIdx.x % kHeads, d = threadIdx.x;
+    const int S = (pos[b] + 1 + kBSplitRows - 1) / kBSplitRows;
+    const float* p = part + (size_t)(b * kHeads + h) * Smax * kBPart;
+    float M = -INFINITY;
+    for (int j = 0; j < S; ++j) M = fmaxf(M, p[(size_t)j * kBPart + kHeadDim]);
+    float Ls = 0.f, acc = 0.f;
+    for (int j = 0; j < S; ++j) {
+        const float mj = p[(size_t)j * kBPart + kHeadDim];
+        if (mj == -INFINITY) continue;
+        const float f = __expf(mj - M);
+        Ls += p[(size_t)j * kBPart + kHeadDim + 1] * f;
+        acc = __fmaf_rn(f, p[(size_t)j * kBPart + d], acc);
+    }
+    att[(size_t)b * kHidden + h * kHeadDim + d] = f2h(acc * __frcp_rn(Ls));
+}
+
+// ---------------------------------------------------------------- ArgMax per row, step bookkeeping
+// kernels/argmax.cuh:7-72 per row (the reference's winner among ties, via argmax_key).
+__global__ void __launch_bounds__(1024) argmax_rows_k(int* __restrict__ out, const half* __restrict__ logits, int V) {
+    __shared__ unsigned long long wk[32];
+    const int ipt = (V + 511) / 512;
+    const uint16_t* lg = reinterpret_cast<const uint16_t*>(logits + (size_t)blockIdx.x * V);
+    unsigned long long best = 0;
+    for (int j = threadIdx.x * 8; j < V; j += 1024 * 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(lg + j);
+        const uint16_t* hh = reinterpret_cast<const uint16_t*>(&u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const unsigned long long k = argmax_key(hh[e], j + e, ipt);
+            best = k > best ? k : best;
+        }
+    }
+    best = warp_max_u64(best);
+    if ((threadIdx.x & 31) == 0) wk[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        best = warp_max_u64(wk[threadIdx.x]);
+        if (threadIdx.x == 0) out[blockIdx.x] = argmax_key_index(best);
+    }
+}
+
+// tok = next, pos += 1, and the step's tokens appended to the output history.
+__global__ void advance_k(int* tok, int* pos, const int* next, int* hist, int* step, int B) {
+    const int b = threadIdx.x;
+    const int s = *step;
+    if (b < B) {
+        hist[(size_t)s * B + b] = next[b];
+        tok[b] = next[b];
+        pos[b] += 1;
+    }
+    __syncthreads();
+    if (b == 0) *step = s + 1;
+}
+
+// Seeded N(0,1) fp16 fill of rows [0, len) of one sequence's cache in every layer
+// (the benchmark's pre-filled ragged KV): counter-based splitmix64 + Box-Muller.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+__global__ void fill_rows_k(half* kc, half* vc, size_t layer_stride, size_t seq_off, int NL, size_t n_per_layer,
+                            uint64_t seed) {
+    const size_t total = (size_t)NL * n_per_layer;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t l = i / n_per_layer, j = i % n_per_layer;
+        const uint64_t r = mix64(seed ^ (i * 0x632BE59BD9B4E019ull));
+        const float u1 = ((uint32_t)(r >> 40) + 1) * (1.0f / 16777217.0f);
+        const float u2 = (uint32_t)(r & 0xFFFFFF) * (1.0f / 16777216.0f);
+        const float rad = sqrtf(-2.0f * logf(u1));
+        const float a = 6.28318530718f * u2;
+        const size_t o = l * layer_stride + seq_off + j;
+        kc[o] = __float2half(rad * cosf(a));
+        vc[o] = __float2half(rad * sinf(a));
+    }
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult qr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+            qr == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+}  // namespace
+
+struct llmdiy_batch {
+    llmdiy_engine* e = nullptr;
+    EngineView v{};
+    int Bmax = 0, max_len = 0, Smax = 0;
+    size_t layer_stride = 0;  // elements per layer of the cache
+    half *kc = nullptr, *vc = nullptr;
+    half *x = nullptr, *xn = nullptr, *q = nullptr, *att = nullptr, *act = nullptr, *logits = nullptr;
+    float* ws = nullptr;
+    size_t ws_floats = 0;
+    float* fdp = nullptr;
+    int *tok = nullptr, *pos = nullptr, *next = nullptr, *hist = nullptr, *step = nullptr, *err = nullptr;
+    int hist_steps = 0;
+    half* pf = nullptr;  // prefill scratch (kPrefillChunk rows)
+    std::vector<CUtensorMap> kmaps, vmaps;  // per layer, over [max_batch * max_len][H]
+    cudaGraphExec_t graph = nullptr;
+    int graph_B = 0;
+    std::string errmsg;
+};
+
+namespace {
+
+int bfail(llmdiy_batch* b, int code, const std::string& m) {
+    if (b) b->errmsg = m;
+    return code;
+}
+#define BCK(call, what)                                                          \
+    do {                                                                         \
+        cudaError_t _e = (call);                                                 \
+        if (_e != cudaSuccess) return bfail(b, (int)_e, std::string(what) + ": " + cudaGetErrorString(_e)); \
+    } while (0)
+
+// Split-K slices so that tiles x slices covers the SMs (every slice non-empty).
+int ksplit_for(int N, int K, int sms) {
+    const int tiles = (N + kGemmBN - 1) / kGemmBN, KB = (K + kGemmBK - 1) / kGemmBK;
+    int z = std::max(1, (sms + tiles / 2) / tiles);
+    z = std::min(z, KB);
+    const int per = (KB + z - 1) / z;
+    return (KB + per - 1) / per;
+}
+
+template <class Epi>
+int gemm_rows(llmdiy_batch* b, const half* A, int lda, const half* W, int N, int K, int M, const Epi& epi,
+              cudaStream_t st) {
+    const int z = ksplit_for(N, K, b->v.num_sms);
+    if (z == 1) return launch_gemm_tc(A, lda, W, K, M, N, K, epi, st);
+    if ((size_t)z * M * N > b->ws_floats) return (int)cudaErrorInvalidValue;
+    int rc = launch_gemm_tc(A, lda, W, K, M, N, K, EpiPartial{b->ws, M, N}, st, z);
+    if (rc) return rc;
+    const int threads = M * (N / 16);
+    splitk_reduce_k<<<(threads + 255) / 256, 256, 0, st>>>(b->ws, z, M, N, epi);
+    return (int)cudaGetLastError();
+}
+
+// One greedy step for sequences 0..B-1 (tok, pos on the device), enqueued on st.
+int enqueue_step(llmdiy_batch* b, int B, cudaStream_t st) {
+    const EngineView& v = b->v;
+    const int NL = (int)v.cfg.num_layers, IM = (int)v.cfg.intermediate_size, V = (int)v.cfg.vocab_size;
+    embed_rows_k<<<B, 256, 0, st>>>(v.wte, b->tok, b->x);
+    for (int l = 0; l < NL; ++l) {
+        const LayerPtrs& L = v.layers[l];
+        half* kcl = b->kc + (size_t)l * b->layer_stride;
+        half* vcl = b->vc + (size_t)l * b->layer_stride;
+        rmsnorm_rows_k<<<B, 256, 0, st>>>(b->xn, b->x, L.ln1);
+        int rc = gemm_rows(b, b->xn, kHidden, L.qkv_w, 3 * kHidden, kHidden, B,
+                           EpiQKVRows{L.qkv_b, b->q, kcl, vcl, b->pos, b->max_len}, st);
+        if (rc) return rc;
+        bfd_partials_k<<<v.num_sms, 128, sizeof(BFdSmem), st>>>(b->kmaps[l], b->vmaps[l], b->q, b->pos, B,
+                                                                 b->max_len, b->Smax, b->fdp, b->err);
+        bfd_merge_k<<<B * kHeads, kHeadDim, 0, st>>>(b->fdp, b->pos, b->Smax, b->att);
+        rc = gemm_rows(b, b->att, kHidden, L.proj_w, kHidden, kHidden, B, EpiResidual{b->x}, st);
+        if (rc) return rc;
+        rmsnorm_rows_k<<<B, 256, 0, st>>>(b->xn, b->x, L.ln2);
+        rc = gemm_rows(b, b->xn, kHidden, L.w12, 2 * IM, kHidden, B, EpiSwiGLU{b->act, IM}, st);
+        if (rc) return rc;
+        rc = gemm_rows(b, b->act, IM, L.cproj, kHidden, IM, B, EpiResidual{b->x}, st);
+        if (rc) return rc;
+    }
+    rmsnorm_rows_k<<<B, 256, 0, st>>>(b->xn, b->x, v.lnf);
+    int rc = gemm_rows(b, b->xn, kHidden, v.lm_head, V, kHidden, B, EpiStoreRows{b->logits, V}, st);
+    if (rc) return rc;
+    argmax_rows_k<<<B, 1024, 0, st>>>(b->next, b->logits, V);
+    advance_k<<<1, kBatchMax, 0, st>>>(b->tok, b->pos, b->next, b->hist, b->step, B);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" {
+
+int llmdiy_batch_create(llmdiy_engine* e, int max_batch, int max_len, llmdiy_batch** out) {
+    if (!e || !out || max_batch <= 0 || max_batch > kBatchMax || max_len <= 0) return LLMDIY_ERR_ARG;
+    *out = nullptr;
+    llmdiy_batch* b = new llmdiy_batch();
+    b->e = e;
+    b->v = engine_view(e);
+    const llmdiy_config& c = b->v.cfg;
+    if (c.vocab_size % 16 || (2 * c.intermediate_size) % 16) {
+        delete b;
+        return LLMDIY_ERR_UNSUPPORTED;
+    }
+    BCK(cudaSetDevice(b->v.device), "cudaSetDevice");
+    b->Bmax = max_batch;
+    b->max_len = max_len;
+    b->Smax = (max_len + kBSplitRows - 1) / kBSplitRows;
+    const size_t H = kHidden, IM = c.intermediate_size, V = c.vocab_size, NL = c.num_layers;
+    b->layer_stride = (size_t)max_batch * max_len * H;
+    int rc = 0;
+    auto alloc = [&](void** p, size_t bytes, const char* what) {
+        if (rc) return;
+        cudaError_t ce = cudaMalloc(p, bytes);
+        if (ce != cudaSuccess) rc = bfail(b, LLMDIY_ERR_NOMEM, std::string(what) + ": " + cudaGetErrorString(ce));
+    };
+    alloc((void**)&b->kc, NL * b->layer_stride * 2, "K caches");
+    alloc((void**)&b->vc, NL * b->layer_stride * 2, "V caches");
+    alloc((void**)&b->x, (size_t)max_batch * H * 2, "x");
+    alloc((void**)&b->xn, (size_t)max_batch * H * 2, "xn");
+    alloc((void**)&b->q, (size_t)max_batch * H * 2, "q");
+    alloc((void**)&b->att, (size_t)max_batch * H * 2, "att");
+    alloc((void**)&b->act, (size_t)max_batch * IM * 2, "act");
+    alloc((void**)&b->logits, (size_t)max_batch * V * 2, "logits");
+    // split-K slices of the largest layer GEMM
+    size_t wsf = 0;
+    const int sms = b->v.num_sms;
+    const int shapes[4][2] = {{3 * kHidden, kHidden}, {kHidden, kHidden}, {(int)(2 * IM), kHidden}, {kHidden, (int)IM}};
+    for (auto& sh : shapes) wsf = std::max(wsf, (size_t)ksplit_for(sh[0], sh[1], sms) * max_batch * sh[0]);
+    wsf = std::max(wsf, (size_t)ksplit_for((int)V, kHidden, sms) * max_batch * V);
+    b->ws_floats = wsf;
+    alloc((void**)&b->ws, wsf * 4, "split-K workspace");
+    alloc((void**)&b->fdp, (size_t)max_batch * kHeads * b->Smax * kBPart * 4, "attention partials");
+    alloc((void**)&b->tok, kBatchMax * 4, "tokens");
+    alloc((void**)&b->pos, kBatchMax * 4, "positions");
+    alloc((void**)&b->next, kBatchMax * 4, "next");
+    alloc((void**)&b->step, 4, "step");
+    alloc((void**)&b->err, 4, "error word");
+    alloc((void**)&b->pf, (size_t)kPrefillChunk * (4 * H + IM) * 2, "prefill scratch");
+    if (!rc) {
+        b->kmaps.resize(NL);
+        b->vmaps.resize(NL);
+        EncodeTiled enc = encode_fn();
+        for (size_t l = 0; l < NL && !rc; ++l) {
+            for (int kv = 0; kv < 2 && !rc; ++kv) {
+                half* base = (kv ? b->vc : b->kc) + l * b->layer_stride;
+                cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)max_batch * max_len};
+                cuuint64_t strides[1] = {(cuuint64_t)H * 2};
+                cuuint32_t box[2] = {(cuuint32_t)kHeadDim, (cuuint32_t)kBRows};
+                cuuint32_t estr[2] = {1, 1};
+                if (!enc || enc(kv ? &b->vmaps[l] : &b->kmaps[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims,
+                                strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                    rc = bfail(b, LLMDIY_ERR_DEVICE, "cuTensorMapEncodeTiled");
+            }
+        }
+    }
+    if (!rc) {
+        cudaError_t ce = cudaFuncSetAttribute(bfd_partials_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)sizeof(BFdSmem));
+        if (ce != cudaSuccess) rc = bfail(b, (int)ce, "smem attribute");
+    }
+    if (!rc) {
+        cudaError_t ce = cudaMemset(b->kc, 0, NL * b->layer_stride * 2);
+        if (ce == cudaSuccess) ce = cudaMemset(b->vc, 0, NL * b->layer_stride * 2);
+        if (ce == cudaSuccess) ce = cudaMemset(b->err, 0, 4);
+        if (ce != cudaSuccess) rc = bfail(b, (int)ce, "clear caches");
+    }
+    if (rc) {
+        std::fprintf(stderr, "[llmdiy] batch create failed: %s\n", b->errmsg.c_str());
+        llmdiy_batch_destroy(b);
+        return rc;
+    }
+    *out = b;
+    return LLMDIY_OK;
+}
+
+void llmdiy_batch_destroy(llmdiy_batch* b) {
+    if (!b) return;
+    cudaSetDevice(b->v.device);
+    if (b->graph) cudaGraphExecDestroy(b->graph);
+    for (void* p : {(void*)b->kc, (void*)b->vc, (void*)b->x, (void*)b->xn, (void*)b->q, (void*)b->att, (void*)b->act,
+                    (void*)b->logits, (void*)b->ws, (void*)b->fdp, (void*)b->tok, (void*)b->pos, (void*)b->next,
+                    (void*)b->hist, (void*)b->step, (void*)b->err, (void*)b->pf})
+        if (p) cudaFree(p);
+    delete b;
+}
+
+const char* llmdiy_batch_last_error(const llmdiy_batch* b) { return b ? b->errmsg.c_str() : "null batch"; }
+
+int llmdiy_batch_fill_random(llmdiy_batch* b, int seq, int len, uint64_t seed) {
+    if (!b || seq < 0 || seq >= b->Bmax || len < 0 || len > b->max_len) return LLMDIY_ERR_ARG;
+    BCK(cudaSetDevice(b->v.device), "cudaSetDevice");
+    if (len == 0) return LLMDIY_OK;
+    const size_t n = (size_t)len * kHidden;
+    fill_rows_k<<<1184, 256, 0, b->v.stream>>>(b->kc, b->vc, b->layer_stride, (size_t)seq * b->max_len * kHidden,
+                                               (int)b->v.cfg.num_layers, n, seed * 0x100000001B3ull + seq);
+    BCK(cudaGetLastError(), "fill");
+    BCK(cudaStreamSynchronize(b->v.stream), "fill");
+    return LLMDIY_OK;
+}
+
+int llmdiy_batch_prefill(llmdiy_batch* b, int seq, const int* tokens, int n) {
+    if (!b || seq < 0 || seq >= b->Bmax || n < 0 || (n > 0 && !tokens) || n > b->max_len) return LLMDIY_ERR_ARG;
+    if (n == 0) return LLMDIY_OK;
+    const llmdiy_config& c = b->v.cfg;
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= (int)c.vocab_size) return bfail(b, LLMDIY_ERR_ARG, "token id out of range");
+    BCK(cudaSetDevice(b->v.device), "cudaSetDevice");
+    int* dtok = nullptr;
+    BCK(cudaMalloc(&dtok, sizeof(int) * n), "prompt buffer");
+    cudaError_t ce = cudaMemcpy(dtok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice);
+    const size_t H = kHidden, R = kPrefillChunk;
+    PrefillArgs p{};
+    p.layers = b->v.layers;
+    p.wte = b->v.wte;
+    p.kc = b->kc + (size_t)seq * b->max_len * H;
+    p.vc = b->vc + (size_t)seq * b->max_len * H;
+    p.layer_stride = b->layer_stride;
+    p.NL = (int)c.num_layers;
+    p.IM = (int)c.intermediate_size;
+    p.max_seqlen = b->max_len;
+    p.x = b->pf;
+    p.xn = p.x + R * H;
+    p.q = p.xn + R * H;
+    p.att = p.q + R * H;
+    p.act = p.att + R * H;
+    p.hidden = b->x + (size_t)seq * H;
+    int rc = ce == cudaSuccess ? prefill_tc(p, dtok, n, 0, b->v.stream) : (int)ce;
+    if (!rc) rc = (int)cudaStreamSynchronize(b->v.stream);
+    cudaFree(dtok);
+    if (rc) return bfail(b, rc, "batch prefill");
+    if (gemm_tc_status()) return bfail(b, LLMDIY_ERR_DEVICE, "prefill GEMM pipeline wait expired");
+    return LLMDIY_OK;
+}
+
+// n_steps greedy steps of sequences 0..B-1 from (tokens[b], pos[b]); tokens_out is [n_steps][B]
+// (host).  The step is captured in a CUDA graph (rebuilt when B changes) and replayed.
+int llmdiy_batch_decode(llmdiy_batch* b, int B, const int* tokens, const int* pos, int n_steps, int* tokens_out,
+                        void* stream) {
+    if (!b || B <= 0 || B > b->Bmax || !tokens || !pos || n_steps < 0 || (n_steps > 0 && !tokens_out))
+        return LLMDIY_ERR_ARG;
+    for (int i = 0; i < B; ++i) {
+        if (tokens[i] < 0 || tokens[i] >= (int)b->v.cfg.vocab_size) return bfail(b, LLMDIY_ERR_ARG, "token id out of range");
+        if (pos[i] < 0 || pos[i] + n_steps > b->max_len) return bfail(b, LLMDIY_ERR_ARG, "position beyond max_len");
+    }
+    BCK(cudaSetDevice(b->v.device), "cudaSetDevice");
+    cudaStream_t st = stream ? reinterpret_cast<cudaStream_t>(stream) : b->v.stream;
+    if (n_steps > b->hist_steps) {
+        if (b->hist) cudaFree(b->hist);
+        b->hist = nullptr;
+        BCK(cudaMalloc(&b->hist, sizeof(int) * (size_t)n_steps * kBatchMax), "token history");
+        b->hist_steps = n_steps;
+        if (b->graph) {  // the graph holds the old history pointer
+            cudaGraphExecDestroy(b->graph);
+            b->graph = nullptr;
+        }
+    }
+    BCK(cudaMemcpyAsync(b->tok, tokens, sizeof(int) * B, cudaMemcpyHostToDevice, st), "tokens");
+    BCK(cudaMemcpyAsync(b->pos, pos, sizeof(int) * B, cudaMemcpyHostToDevice, st), "positions");
+    BCK(cudaMemsetAsync(b->step, 0, 4, st), "step");
+    if (n_steps == 0) return LLMDIY_OK;
+    int first = 0;
+    if (!b->graph || b->graph_B != B) {
+        // the first step runs eagerly (this also performs every one-time set-up of the kernels it
+        // launches), then the step is captured for the remaining ones
+        int rc0 = enqueue_step(b, B, st);
+        if (rc0) return bfail(b, rc0, "batched step");
+        first = 1;
+        if (b->graph) cudaGraphExecDestroy(b->graph);
+        b->graph = nullptr;
+        cudaStream_t cap;
+        BCK(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking), "capture stream");
+        cudaGraph_t g = nullptr;
+        cudaError_t ce = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+        int rc = ce == cudaSuccess ? enqueue_step(b, B, cap) : (int)ce;
+        cudaError_t ce2 = cudaStreamEndCapture(cap, &g);
+        if (!rc && ce2 != cudaSuccess) rc = (int)ce2;
+        if (!rc) rc = (int)cudaGraphInstantiate(&b->graph, g, 0);
+        if (g) cudaGraphDestroy(g);
+        cudaStreamDestroy(cap);
+        if (rc) return bfail(b, rc, "capture of the batched step");
+        b->graph_B = B;
+    }
+    for (int s = first; s < n_steps; ++s) BCK(cudaGraphLaunch(b->graph, st), "step launch");
+    BCK(cudaMemcpyAsync(tokens_out, b->hist, sizeof(int) * (size_t)n_steps * B, cudaMemcpyDeviceToHost, st),
+        "tokens out");
+    BCK(cudaStreamSynchronize(st), "batch decode");
+    int err = 0;
+    BCK(cudaMemcpy(&err, b->err, 4, cudaMemcpyDeviceToHost), "error word");
+    if (err) return bfail(b, LLMDIY_ERR_DEVICE, "batched attention pipeline wait expired");
+    if (gemm_tc_status()) return bfail(b, LLMDIY_ERR_DEVICE, "batched GEMM pipeline wait expired");
+    return LLMDIY_OK;
+}
+
+int llmdiy_batch_copy_logits(llmdiy_batch* b, int seq, uint16_t* out) {
+    if (!b || !out || seq < 0 || seq >= b->Bmax) return LLMDIY_ERR_ARG;
+    BCK(cudaSetDevice(b->v.device), "cudaSetDevice");
+    BCK(cudaMemcpy(out, b->logits + (size_t)seq * b->v.cfg.vocab_size, (size_t)b->v.cfg.vocab_size * 2,
+                   cudaMemcpyDeviceToHost), "copy logits");
+    return LLMDIY_OK;
+}
+
+int llmdiy_batch_copy_kv(llmdiy_batch* b, int seq, int layer, int pos0, int n, uint16_t* k, uint16_t* v) {
+    if (!b || seq < 0 || seq >= b->Bmax || layer < 0 || layer >= (int)b->v.cfg.num_layers || pos0 < 0 || n < 0 ||
+        pos0 + n > b->max_len)
+        return LLMDIY_ERR_ARG;
+    BCK(cudaSetDevice(b->v.device), "cudaSetDevice");
+    const size_t off = (size_t)layer * b->layer_stride + ((size_t)seq * b->max_len + pos0) * kHidden;
+    if (k) BCK(cudaMemcpy(k, b->kc + off, (size_t)n * kHidden * 2, cudaMemcpyDeviceToHost), "copy K");
+    if (v) BCK(cudaMemcpy(v, b->vc + off, (size_t)n * kHidden * 2, cudaMemcpyDeviceToHost), "copy V");
+    return LLMDIY_OK;
+}
+
+}  // extern "C"

@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "decode.h"
+#include "engine_internal.h"
 #include "gemm_tc_host.h"
 #include "llmdiy_engine.h"
 #include "prefill_tc.h"
@@ -414,6 +415,7 @@ int prefill_impl(llmdiy_engine* e, const int* tokens, int n) {
     p.NL = (int)c.num_layers;
     p.IM = (int)c.intermediate_size;
     p.max_seqlen = (int)c.max_seqlen;
+    p.layer_stride = (size_t)c.max_seqlen * H;
     p.x = e->pf;
     p.xn = p.x + R * H;
     p.q = p.xn + R * H;
@@ -428,6 +430,21 @@ int prefill_impl(llmdiy_engine* e, const int* tokens, int n) {
 }
 
 }  // namespace
+
+namespace llmdiy {
+EngineView engine_view(const llmdiy_engine* e) {
+    EngineView v{};
+    v.cfg = e->cfg;
+    v.device = e->device;
+    v.num_sms = e->num_sms;
+    v.stream = e->stream;
+    v.layers = e->layers.data();
+    v.wte = e->wte;
+    v.lnf = e->lnf;
+    v.lm_head = e->lm_head;
+    return v;
+}
+}  // namespace llmdiy
 
 extern "C" {
 

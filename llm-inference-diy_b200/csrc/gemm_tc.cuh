@@ -46,7 +46,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     GemmSmem<BN>& s = *reinterpret_cast<GemmSmem<BN>*>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int m0 = blockIdx.y * kGemmBM, n0 = blockIdx.x * BN;
-    const int KB = (K + kGemmBK - 1) / kGemmBK;
+    // split-K: z-slice blockIdx.z of gridDim.z takes K blocks [kb0, kb0 + KB) (the host makes
+    // every slice non-empty); the epilogue then writes a partial sum
+    const int KBall = (K + kGemmBK - 1) / kGemmBK;
+    const int per = (KBall + (int)gridDim.z - 1) / (int)gridDim.z;
+    const int kb0 = (int)blockIdx.z * per;
+    const int KB = min(per, KBall - kb0);
     constexpr uint32_t kStageBytes = (kGemmBM + BN) * kGemmBK * 2;
     constexpr uint32_t kCols = BN < 32 ? 32 : BN;  // TMEM columns: a power of two >= 32
     if (tid == 0) {
@@ -76,8 +81,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 break;
             }
             mbar_arrive_expect_tx(&s.full[st], kStageBytes);
-            tma_load_2d(s.a[st], &tma, kb * kGemmBK, m0, &s.full[st]);
-            tma_load_2d(s.b[st], &tmb, kb * kGemmBK, n0, &s.full[st]);
+            tma_load_2d(s.a[st], &tma, (kb0 + kb) * kGemmBK, m0, &s.full[st]);
+            tma_load_2d(s.b[st], &tmb, (kb0 + kb) * kGemmBK, n0, &s.full[st]);
             ++issued;
         }
     } else if (warp == 1 && lane == 0) {

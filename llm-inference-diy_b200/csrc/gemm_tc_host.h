@@ -17,9 +17,10 @@ int* gemm_err_word();  // per-device error word of the GEMM kernels (set when a 
 int gemm_tc_status();  // 0, or 1 once any GEMM of this device recorded an expired wait
 
 // C tile op `epi` is called per thread with (row, first column, 16 fp32 values).
+// ksplit > 1: grid.z slices of the K blocks, each running `epi` on its partial sums.
 template <class Epi>
 int launch_gemm_tc(const half* A, int lda, const half* W, int ldw, int M, int N, int K, const Epi& epi,
-                   cudaStream_t st) {
+                   cudaStream_t st, int ksplit = 1) {
     if (M <= 0 || N <= 0 || K <= 0) return (int)cudaErrorInvalidValue;
     constexpr int BN = kGemmBN;
     CUtensorMap ta, tb;
@@ -32,7 +33,11 @@ int launch_gemm_tc(const half* A, int lda, const half* W, int ldw, int M, int N,
     std::call_once(attr, [&] {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(GemmSmem<BN>));
     });
-    dim3 grid((N + BN - 1) / BN, (M + kGemmBM - 1) / kGemmBM);
+    const int KB = (K + kGemmBK - 1) / kGemmBK;
+    if (ksplit < 1 || ksplit > KB) return (int)cudaErrorInvalidValue;
+    const int per = (KB + ksplit - 1) / ksplit;
+    if ((ksplit - 1) * per >= KB) return (int)cudaErrorInvalidValue;  // an empty slice
+    dim3 grid((N + BN - 1) / BN, (M + kGemmBM - 1) / kGemmBM, ksplit);
     kern<<<grid, kGemmThreads, sizeof(GemmSmem<BN>), st>>>(ta, tb, M, N, K, epi, err);
     return (int)cudaGetLastError();
 }

@@ -19,31 +19,10 @@
 #include "gemm_tc_host.h"
 #include "ops.cuh"
 #include "prefill_tc.h"
+#include "rows.cuh"
 
 namespace llmdiy {
 namespace {
-
-__global__ void __launch_bounds__(256) embed_rows_k(const half* __restrict__ wte, const int* __restrict__ tokens,
-                                                    half* __restrict__ x) {
-    const int r = blockIdx.x, t = threadIdx.x;
-    const half* src = wte + (size_t)tokens[r] * kHidden;
-    *reinterpret_cast<uint4*>(x + (size_t)r * kHidden + 8 * t) = *reinterpret_cast<const uint4*>(src + 8 * t);
-}
-
-// out = half((x * r) * w) per row with the reference's reduction tree (rmsnorm.cuh:6-57)
-__global__ void __launch_bounds__(256) rmsnorm_rows_k(half* __restrict__ out, const half* __restrict__ x,
-                                                      const half* __restrict__ w) {
-    __shared__ float red[17];
-    const int r = blockIdx.x, t = threadIdx.x;
-    const half* xr = x + (size_t)r * kHidden;
-    const float s = rms_scale_tree256(xr, kHidden, 1e-6f, red, t, 1);
-    float xf[8], wf[8], of[8];
-    unpack8(*reinterpret_cast<const uint4*>(xr + 8 * t), xf);
-    unpack8(*reinterpret_cast<const uint4*>(w + 8 * t), wf);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) of[e] = (xf[e] * s) * wf[e];
-    *reinterpret_cast<uint4*>(out + (size_t)r * kHidden + 8 * t) = pack8(of);
-}
 
 // QKV epilogue: columns (2u, 2u+1) are RoPE partners (t, t+64) of unit u =
 // sec*1024 + h*64 + t.  bias -> RoPE (q, k) -> q kept in [row][H], k and v
@@ -90,44 +69,6 @@ struct EpiQKV {
     }
 };
 
-// x[row][n..n+15] = half(x + half(acc))  (the residual adds, bias.cuh:6-11)
-struct EpiResidual {
-    half* x;
-    __device__ void operator()(int row, int n, const float* v) const {
-        half* p = x + (size_t)row * kHidden + n;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            float xf[8], of[8];
-            unpack8(*reinterpret_cast<const uint4*>(p + 8 * k), xf);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) of[e] = xf[e] + h2f(f2h(v[8 * k + e]));
-            *reinterpret_cast<uint4*>(p + 8 * k) = pack8(of);
-        }
-    }
-};
-
-// SwiGLU epilogue: columns (2u, 2u+1) = (w1 row u, w2 row u); act = half(g * up / (1 + e^-up))
-// with g, up the fp16-rounded GEMM outputs (swiglu.cuh:6-15).
-struct EpiSwiGLU {
-    half* act;
-    int IM;
-    __device__ void operator()(int row, int n, const float* v) const {
-        const int u0 = n >> 1;
-        float of[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float g = h2f(f2h(v[2 * j])), up = h2f(f2h(v[2 * j + 1]));
-            of[j] = g * __fdividef(up, 1.0f + __expf(-up));
-        }
-        half* dst = act + (size_t)row * IM + u0;
-        if (u0 + 8 <= IM && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-            *reinterpret_cast<uint4*>(dst) = pack8(of);
-        } else {
-            for (int j = 0; j < 8 && u0 + j < IM; ++j) dst[j] = f2h(of[j]);
-        }
-    }
-};
-
 }  // namespace
 
 int prefill_tc(const PrefillArgs& p, const int* tokens_dev, int n, int p0, cudaStream_t st) {
@@ -144,8 +85,8 @@ int prefill_tc(const PrefillArgs& p, const int* tokens_dev, int n, int p0, cudaS
         embed_rows_k<<<m, 256, 0, st>>>(p.wte, tokens_dev + c0, p.x);
         for (int l = 0; l < p.NL; ++l) {
             const LayerPtrs& L = p.layers[l];
-            half* kcl = p.kc + (size_t)l * p.max_seqlen * kHidden;
-            half* vcl = p.vc + (size_t)l * p.max_seqlen * kHidden;
+            half* kcl = p.kc + (size_t)l * p.layer_stride;
+            half* vcl = p.vc + (size_t)l * p.layer_stride;
             rmsnorm_rows_k<<<m, 256, 0, st>>>(p.xn, p.x, L.ln1);
             rc = launch_gemm_tc(p.xn, kHidden, L.qkv_w, kHidden, m, 3 * kHidden, kHidden,
                                 EpiQKV{L.qkv_b, p.q, kcl, vcl, pos0}, st);

@@ -12,8 +12,9 @@ constexpr int kPrefillChunk = 2048;  // prompt rows per pass (scratch is sized f
 struct PrefillArgs {
     const LayerPtrs* layers;  // host array [NL] of device pointers
     const half* wte;
-    half* kc;
+    half* kc;                  // layer l of the cache at kc + l * layer_stride, row r at + r * H
     half* vc;
+    size_t layer_stride;       // elements between layers of the cache
     int NL, IM, max_seqlen;
     // scratch, kPrefillChunk rows each: x, xn, q, att [rows][H]; act [rows][IM]
     half *x, *xn, *q, *att, *act;

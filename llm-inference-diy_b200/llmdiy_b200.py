@@ -113,6 +113,22 @@ def lib() -> ctypes.CDLL:
     L.llmdiy_engine_destroy.restype = None
     L.llmdiy_engine_last_error.argtypes = [P]
     L.llmdiy_engine_last_error.restype = ctypes.c_char_p
+    bsig = {
+        "llmdiy_batch_create": [P, I, I, ctypes.POINTER(ctypes.c_void_p)],
+        "llmdiy_batch_fill_random": [P, I, I, U64],
+        "llmdiy_batch_prefill": [P, I, IP, I],
+        "llmdiy_batch_decode": [P, I, IP, IP, I, IP, P],
+        "llmdiy_batch_copy_logits": [P, I, P],
+        "llmdiy_batch_copy_kv": [P, I, I, I, I, P, P],
+    }
+    for name, args in bsig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_int
+    L.llmdiy_batch_destroy.argtypes = [P]
+    L.llmdiy_batch_destroy.restype = None
+    L.llmdiy_batch_last_error.argtypes = [P]
+    L.llmdiy_batch_last_error.restype = ctypes.c_char_p
     L.llmdiy_fd_mh_work_bytes.argtypes = [I, I]
     L.llmdiy_fd_mh_work_bytes.restype = SZ
     _lib = L
@@ -365,3 +381,62 @@ class Engine:
     @property
     def num_sms(self) -> int:
         return lib().llmdiy_engine_num_sms(self._h)
+
+
+class Batch:
+    """Batched greedy decode of independent sequences on an Engine's weights (include/llmdiy_batch.h)."""
+
+    def __init__(self, engine: "Engine", max_batch: int, max_len: int):
+        self.engine = engine  # keeps the weights alive
+        self._h = ctypes.c_void_p()
+        self.max_batch, self.max_len = max_batch, max_len
+        rc = lib().llmdiy_batch_create(engine._h, max_batch, max_len, ctypes.byref(self._h))
+        if rc:
+            raise LlmdiyError(f"batch create failed with status {rc}")
+
+    def _chk(self, rc, what):
+        if rc:
+            m = lib().llmdiy_batch_last_error(self._h)
+            raise LlmdiyError(f"{what} failed with status {rc} {m.decode() if m else ''}".strip())
+
+    def close(self):
+        if self._h:
+            lib().llmdiy_batch_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def fill_random(self, seq: int, length: int, seed: int):
+        self._chk(lib().llmdiy_batch_fill_random(self._h, seq, length, seed), "batch fill_random")
+
+    def prefill(self, seq: int, tokens):
+        self._chk(lib().llmdiy_batch_prefill(self._h, seq, _ints(tokens), len(tokens)), "batch prefill")
+
+    def decode(self, tokens, pos, n_steps: int, stream=None):
+        """n_steps greedy steps of len(tokens) sequences; returns an int array [n_steps][B]."""
+        import numpy as np
+        B = len(tokens)
+        out = (ctypes.c_int * max(1, n_steps * B))()
+        self._chk(lib().llmdiy_batch_decode(self._h, B, _ints(tokens), _ints(pos), n_steps, out, _p(stream)),
+                  "batch decode")
+        return np.frombuffer(out, dtype=np.int32)[: n_steps * B].reshape(n_steps, B).copy()
+
+    def logits(self, seq: int):
+        import numpy as np
+        V = self.engine.config.vocab_size
+        out = np.zeros(V, dtype=np.uint16)
+        self._chk(lib().llmdiy_batch_copy_logits(self._h, seq, out.ctypes.data_as(ctypes.c_void_p)), "batch logits")
+        return out.view(np.float16)
+
+    def kv(self, seq: int, layer: int, pos0: int, n: int):
+        import numpy as np
+        H = self.engine.config.hidden_size
+        k = np.zeros(n * H, dtype=np.uint16)
+        v = np.zeros(n * H, dtype=np.uint16)
+        self._chk(lib().llmdiy_batch_copy_kv(self._h, seq, layer, pos0, n, k.ctypes.data_as(ctypes.c_void_p),
+                                             v.ctypes.data_as(ctypes.c_void_p)), "batch kv")
+        return k.view(np.float16).reshape(n, H), v.view(np.float16).reshape(n, H)
