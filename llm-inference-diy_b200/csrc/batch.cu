@@ -40,7 +40,7 @@ namespace {
 
 constexpr int kBatchMax = 64;
 constexpr int kBRows = 64;   // KV rows per TMA tile
-constexpr int kBSplitRows = 512;  // KV rows per attention work item
+constexpr int kBSplitRows = 1024;  // KV rows per attention work item
 constexpr int kBStages = 6;
 constexpr int kBPart = kHeadDim + 2;
 
@@ -108,27 +108,34 @@ struct EpiStoreRows {
 };
 
 // Sum the split-K slices of one (row, 16 columns) in slice order and apply `epi`.
+// Four threads share a 16-column group (4 columns each, one float4 load per
+// slice), then lane 4k of the quad gathers the 16 sums and runs the op.
 template <class Epi>
 __global__ void __launch_bounds__(256) splitk_reduce_k(const float* __restrict__ ws, int Z, int M, int N, Epi epi) {
     const int groups = N / 16;
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= M * groups) return;
-    const int row = idx / groups, n = (idx % groups) * 16;
-    float acc[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-    for (int z = 0; z < Z; ++z) {
-        const float* p = ws + ((size_t)z * M + row) * N + n;
-#pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-            const float4 f = *reinterpret_cast<const float4*>(p + j);
-            acc[j] += f.x;
-            acc[j + 1] += f.y;
-            acc[j + 2] += f.z;
-            acc[j + 3] += f.w;
+    const int gidx = (blockIdx.x * blockDim.x + threadIdx.x) >> 2, part = threadIdx.x & 3;
+    const bool live = gidx < M * groups;  // the quad is warp-aligned: all four lanes agree
+    const int row = live ? gidx / groups : 0, n = live ? (gidx % groups) * 16 : 0;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (live) {
+        for (int z = 0; z < Z; ++z) {
+            const float4 f = *reinterpret_cast<const float4*>(ws + ((size_t)z * M + row) * N + n + 4 * part);
+            acc.x += f.x;
+            acc.y += f.y;
+            acc.z += f.z;
+            acc.w += f.w;
         }
     }
-    epi(row, n, acc);
+    float v[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int src = (threadIdx.x & ~3) + q;
+        v[4 * q] = __shfl_sync(0xffffffffu, acc.x, src & 31);
+        v[4 * q + 1] = __shfl_sync(0xffffffffu, acc.y, src & 31);
+        v[4 * q + 2] = __shfl_sync(0xffffffffu, acc.z, src & 31);
+        v[4 * q + 3] = __shfl_sync(0xffffffffu, acc.w, src & 31);
+    }
+    if (live && part == 0) epi(row, n, v);
 }
 
 // ---------------------------------------------------------------- ragged split-KV attention
@@ -140,6 +147,7 @@ struct BFdSmem {
     float sm[4], sl[4];
     int pre[kBatchMax + 1];  // prefix sums of the items per sequence
     int nsp[kBatchMax];      // splits per sequence
+    int len[kBatchMax];      // rows attended per sequence (pos + 1)
 };
 
 struct BItem {
@@ -147,7 +155,7 @@ struct BItem {
     int tile, ntiles;
 };
 
-__device__ __forceinline__ void bfd_item(const BFdSmem& s, int item, int B, const int* pos, BItem& it) {
+__device__ __forceinline__ void bfd_item(const BFdSmem& s, int item, int B, BItem& it) {
     int b = 0;
     while (b + 1 < B && s.pre[b + 1] <= item) ++b;
     const int r = item - s.pre[b], S = s.nsp[b];
@@ -155,7 +163,7 @@ __device__ __forceinline__ void bfd_item(const BFdSmem& s, int item, int B, cons
     it.h = r / S;
     it.sp = r % S;
     it.r0 = it.sp * kBSplitRows;
-    it.r1 = min(pos[b] + 1, it.r0 + kBSplitRows);
+    it.r1 = min(s.len[b], it.r0 + kBSplitRows);
     it.tile = 0;
     it.ntiles = (it.r1 - it.r0 + kBRows - 1) / kBRows;
 }
@@ -175,7 +183,8 @@ __global__ void __launch_bounds__(128, 1)
         mbar_fence_init();
         int acc = 0;
         for (int b = 0; b < B; ++b) {
-            const int S = (pos[b] + 1 + kBSplitRows - 1) / kBSplitRows;
+            s.len[b] = pos[b] + 1;
+            const int S = (s.len[b] + kBSplitRows - 1) / kBSplitRows;
             s.nsp[b] = S;
             s.pre[b] = acc;
             acc += S * kHeads;
@@ -186,14 +195,14 @@ __global__ void __launch_bounds__(128, 1)
     const int nitems = s.pre[B], G = gridDim.x;
     BItem pc;
     uint32_t issued = 0, consumed = 0;
-    if (tid == 0 && (int)blockIdx.x < nitems) bfd_item(s, blockIdx.x, B, pos, pc);
+    if (tid == 0 && (int)blockIdx.x < nitems) bfd_item(s, blockIdx.x, B, pc);
     else pc.b = -1;
     auto produce = [&]() {
         if (pc.b < 0) return;
         while (pc.tile >= pc.ntiles) {
             const int nxt = (int)(s.pre[pc.b] + pc.h * s.nsp[pc.b] + pc.sp) + G;  // this item's index + G
             if (nxt >= nitems) { pc.b = -1; return; }
-            bfd_item(s, nxt, B, pos, pc);
+            bfd_item(s, nxt, B, pc);
         }
         const int st = issued % kBStages;
         const int y = pc.b * max_len + pc.r0 + pc.tile * kBRows;
@@ -209,7 +218,7 @@ __global__ void __launch_bounds__(128, 1)
     bool failed = false;
     for (int item = blockIdx.x; item < nitems && !failed; item += G) {
         BItem it;
-        bfd_item(s, item, B, pos, it);
+        bfd_item(s, item, B, it);
         float q8[8];
         unpack8(*reinterpret_cast<const uint4*>(q + (size_t)it.b * kHidden + it.h * kHeadDim + dl), q8);
         float m = -INFINITY, l = 0.f, o8[8];
@@ -443,7 +452,7 @@ int gemm_rows(llmdiy_batch* b, const half* A, int lda, const half* W, int N, int
     if ((size_t)z * M * N > b->ws_floats) return (int)cudaErrorInvalidValue;
     int rc = launch_gemm_tc(A, lda, W, K, M, N, K, EpiPartial{b->ws, M, N}, st, z);
     if (rc) return rc;
-    const int threads = M * (N / 16);
+    const int threads = 4 * M * (N / 16);
     splitk_reduce_k<<<(threads + 255) / 256, 256, 0, st>>>(b->ws, z, M, N, epi);
     return (int)cudaGetLastError();
 }
