@@ -64,35 +64,59 @@ __device__ __forceinline__ void fma2_f16(float& acc0, float& acc1, uint32_t w, u
         : "r"(w), "r"(x));
 }
 
-// fp32-accumulated dot products of two weight rows (a unit) against the
-// activation: K = 2048 with the lane's 64-element fp16 activation slice in
-// registers (xh: 32 half pairs), or any K with the activation in shared
-// memory.  After the butterfly every lane holds both sums.
-__device__ __forceinline__ void dot2_regs(const half* r0, const half* r1, const uint32_t* xh, int lane, float& s0,
-                                          float& s1) {
-    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+
+// The three units (six rows of K = 2048) of a chunk against the lane's
+// activation slice in registers, all rows at once for load/FMA parallelism,
+// then a transposing butterfly (9 shuffles for 6 sums instead of 30): lane
+// 8j ends with unit j's two dot products (rows 2j, 2j+1).  Rows past the
+// chunk's units read stale slot data and are ignored.
+__device__ __forceinline__ void dot6_regs(const half* buf, const uint32_t* xh, int lane, float& s0, float& s1) {
+    float a[6][2];
+#pragma unroll
+    for (int r = 0; r < 6; ++r) a[r][0] = a[r][1] = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const uint4 w0 = *reinterpret_cast<const uint4*>(r0 + 256 * j + 8 * lane);
-        const uint4 w1 = *reinterpret_cast<const uint4*>(r1 + 256 * j + 8 * lane);
-        fma2_f16(a0, a1, w0.x, xh[4 * j + 0]);
-        fma2_f16(b0, b1, w1.x, xh[4 * j + 0]);
-        fma2_f16(a0, a1, w0.y, xh[4 * j + 1]);
-        fma2_f16(b0, b1, w1.y, xh[4 * j + 1]);
-        fma2_f16(a0, a1, w0.z, xh[4 * j + 2]);
-        fma2_f16(b0, b1, w1.z, xh[4 * j + 2]);
-        fma2_f16(a0, a1, w0.w, xh[4 * j + 3]);
-        fma2_f16(b0, b1, w1.w, xh[4 * j + 3]);
-    }
-    s0 = a0 + a1;
-    s1 = b0 + b1;
+        uint4 w[6];
 #pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) {
-        s0 += __shfl_xor_sync(0xffffffffu, s0, m);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, m);
+        for (int r = 0; r < 6; ++r) w[r] = *reinterpret_cast<const uint4*>(buf + r * kHidden + 256 * j + 8 * lane);
+#pragma unroll
+        for (int r = 0; r < 6; ++r) {
+            fma2_f16(a[r][0], a[r][1], w[r].x, xh[4 * j + 0]);
+            fma2_f16(a[r][0], a[r][1], w[r].y, xh[4 * j + 1]);
+            fma2_f16(a[r][0], a[r][1], w[r].z, xh[4 * j + 2]);
+            fma2_f16(a[r][0], a[r][1], w[r].w, xh[4 * j + 3]);
+        }
     }
+    float v[8];
+#pragma unroll
+    for (int r = 0; r < 6; ++r) v[r] = a[r][0] + a[r][1];
+    v[6] = v[7] = 0.f;
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+    float t[4], u[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float send = b4 ? v[i] : v[i + 4], keep = b4 ? v[i + 4] : v[i];
+        t[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float send = b3 ? t[i] : t[i + 2], keep = b3 ? t[i + 2] : t[i];
+        u[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    float w;
+    {
+        const float send = b2 ? u[0] : u[1], keep = b2 ? u[1] : u[0];
+        w = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    w += __shfl_xor_sync(0xffffffffu, w, 2);
+    w += __shfl_xor_sync(0xffffffffu, w, 1);
+    // lane l now holds row 4*b4 + 2*b3 + b2; the partner row of a unit sits 4 lanes up
+    s0 = w;
+    s1 = __shfl_down_sync(0xffffffffu, w, 4);
 }
 
+// fp32-accumulated dot products of two weight rows (a unit) of any K against
+// the activation in shared memory; after the butterfly every lane holds both.
 __device__ __forceinline__ void dot2_smem(const half* r0, const half* r1, const half* xs, int K, int lane, float& s0,
                                           float& s1) {
     float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
@@ -438,27 +462,32 @@ __device__ __forceinline__ void gemv_phase(int PH, const DecodeArgs& a, Smem& s,
             continue;
         }
         const unsigned long long t1 = a.prof_prod ? (unsigned long long)clock64() : 0ull;
-        // QKV: the bias pair of unit `lane` is fetched before the dot products
+        // the unit whose epilogue this lane runs: lane 8j after dot6_regs, lane j after dot2_smem
+        const int ej = PH == PH_C ? (lane < nun ? lane : -1) : (((lane & 7) == 0 && (lane >> 3) < nun) ? lane >> 3 : -1);
+        // QKV: the bias pair of that unit is fetched before the dot products
         float b0 = 0.f, b1 = 0.f;
         if (PH == PH_QKV) {
-            if (lane < nun) {
-                const int u = cu + lane, sec = u / (kHidden / 2), v = u % (kHidden / 2);
+            if (ej >= 0) {
+                const int u = cu + ej, sec = u / (kHidden / 2), v = u % (kHidden / 2);
                 const int i1 = sec * kHidden + (v / 64) * kHeadDim + (v % 64);
                 b0 = h2f(c.bias[i1]);
                 b1 = h2f(c.bias[i1 + 64]);
             }
         }
         const half* buf = reinterpret_cast<const half*>(s.ring[warp]);
-        float r0s = 0.f, r1s = 0.f;  // lane j keeps unit j's two dot products
+        float r0s = 0.f, r1s = 0.f;  // the epilogue lane's two dot products
+        if (PH == PH_C) {
 #pragma unroll 1
-        for (int j = 0; j < nun; ++j) {
-            const half* r0 = buf + (size_t)j * 2 * K;
-            float s0, s1;
-            if (PH == PH_C) dot2_smem(r0, r0 + K, s.act, K, lane, s0, s1);
-            else dot2_regs(r0, r0 + K, xr, lane, s0, s1);
-            if (lane == j) { r0s = s0; r1s = s1; }
+            for (int j = 0; j < nun; ++j) {
+                const half* r0 = buf + (size_t)j * 2 * K;
+                float s0, s1;
+                dot2_smem(r0, r0 + K, s.act, K, lane, s0, s1);
+                if (lane == j) { r0s = s0; r1s = s1; }
+            }
+        } else {
+            dot6_regs(buf, xr, lane, r0s, r1s);
         }
-        if (lane < nun) epilogue(PH, a, s, c, cu + lane, r0s, r1s, b0, b1);
+        if (ej >= 0) epilogue(PH, a, s, c, cu + ej, r0s, r1s, b0, b1);
         __syncwarp();
         const unsigned long long t2 = a.prof_prod ? (unsigned long long)clock64() : 0ull;
         // the slot is drained: stream this warp's next chunk into it
@@ -732,7 +761,7 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
             continue;
         }
         // argmax over the CTAs' best keys (argmax.cuh tie rule, see argmax_key)
-        c.best = warp_max_u64(c.best);  // lanes 0..2 each tracked their own units
+        c.best = warp_max_u64(c.best);  // the epilogue lanes each tracked their own units
         if (lane == 0) s.wkey[warp] = c.best;
         named_bar_sync(1, 256);
         if (tid == 0) {
