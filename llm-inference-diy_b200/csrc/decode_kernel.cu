@@ -176,7 +176,7 @@ __device__ __forceinline__ bool ll_read(const unsigned long long* p, int stride,
             }
         }
         if (!pending) return true;
-        __nanosleep(it < 8 ? 32 : 128);
+        __nanosleep(16);
     }
     return false;
 }
@@ -197,7 +197,7 @@ __device__ __forceinline__ bool ll_read_n(const unsigned long long* p, int strid
             }
         }
         if (!pending) return true;
-        __nanosleep(it < 8 ? 32 : 128);
+        __nanosleep(16);
     }
     return false;
 }
@@ -225,7 +225,7 @@ __device__ __forceinline__ bool ll_gather_act(const unsigned long long* p, int n
             }
         }
         if (!pending) return true;
-        __nanosleep(it < 8 ? 32 : 128);
+        __nanosleep(16);
     }
     return false;
 }
