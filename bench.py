@@ -168,8 +168,9 @@ def barrier(pg, local):
 
 
 # ------------------------------------------------------------------ CPU baseline (oracle port)
-def cpu_decode_sample(n_tokens, threads):
-    """Time n_tokens decode steps of the CPU restatement on the same weights (tokens/s)."""
+def cpu_decode_sample(n_tokens, threads, warm_tokens=1):
+    """Time n_tokens decode steps of the CPU restatement on the same weights (tokens/s), after
+    warm_tokens untimed steps."""
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import llmdiy_b200 as L
@@ -185,7 +186,8 @@ def cpu_decode_sample(n_tokens, threads):
     # rows it attends over are the zero-initialised cache, which costs the same work.
     p = prompt_ids()
     tok, pos = p[-1], PROMPT_LEN - 1
-    m.step(p[0], 0)  # touch every weight page once
+    for i in range(max(1, warm_tokens)):
+        m.step(p[i % len(p)], i % PROMPT_LEN)  # touch every weight page; untimed
     t0 = time.perf_counter()
     for _ in range(n_tokens):
         tok, _, _ = m.step(tok, pos)
@@ -199,15 +201,16 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    n_per = 2
-    rate, dt = cpu_decode_sample(n_per * args.steps, threads)
+    n_per = 8  # decode tokens per step: a bounded sample of the 256-token workload
+    rate, dt = cpu_decode_sample(n_per * args.steps, threads, warm_tokens=n_per * max(1, args.warmup))
     line = {
         "impl": "reference", "metric": "decode_tokens_per_s", "value": round(rate, 4), "unit": "tok/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * dt / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (fp16 storage)",
         "data": "synthetic: seeded N(0,0.02) fp16 weights, uniform random prompt ids",
-        "config": {"workload": "Qwen-1.8B bs1 greedy decode, prompt 128, 256 new tokens",
-                   "sample": f"{n_per} decode tokens per step at positions 127.."},
+        "config": {"workload": "Qwen-1.8B bs1 greedy decode: prompt 128, 256 new tokens (BASELINE configs[1])",
+                   "sample": f"{n_per} decode tokens per step at positions 127.., {n_per * max(1, args.warmup)} "
+                             f"untimed warm-up tokens"},
         "cpu_baseline": {"value": round(rate, 4), "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": f"{n_per * args.steps} decode tokens of the Qwen-1.8B workload, fp32 C "
                                    f"restatement (oracle/qwen_oracle.c), {threads} threads"},
@@ -583,8 +586,8 @@ def run_gemm(args, rank, world, local, pg):
 
 def run_ncu_case():
     """Small case for ncu captures of decode_kernel: the Qwen-1.8B shapes with 4 layers (full vocab,
-    0.95 GB of weights, larger than L2), one prefill launch of 127 tokens, then one decode launch of
-    2 tokens (capture it with `-k regex:decode_kernel -s 1 -c 1`)."""
+    0.95 GB of weights, larger than L2), a tensor-core prefill of 127 tokens, then one decode_kernel
+    launch of 2 tokens (capture it with `-k regex:decode_kernel -c 1`)."""
     import torch
     import llmdiy_b200 as L
     cfg = L.make_config(**dict(QWEN, num_layers=4), max_seqlen=MAX_SEQLEN)
@@ -607,7 +610,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-tokens", type=int, default=8)
+    ap.add_argument("--cpu-tokens", type=int, default=256,
+                    help="decode tokens of the CPU baseline sample (256 = the whole workload, ~15 s on 16 cores)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu-case", action="store_true", help="run the small decode case used for ncu captures")
     ap.add_argument("--workload", default="decode", choices=["decode", "fd-op", "prefill", "gemm", "batch"],
