@@ -31,6 +31,7 @@ namespace {
 enum PhaseId { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_W12 = 3, PH_C = 4, PH_LM = 5 };
 
 constexpr int kMaxIM = 6144;
+constexpr int kQkvBiasUnits = 64;  // QKV units per CTA whose bias pairs are staged in shared memory
 constexpr uint32_t kPollLimit = 1u << 21;  // polls of one flag-carrying word or of the step barrier
 
 struct __align__(128) Smem {
@@ -46,6 +47,7 @@ struct __align__(128) Smem {
     uint64_t full[kRingStages];
     LayerPtrs layers[kMaxLayers];  // copy of a.layers (read at every phase change)
     int range[5][4];               // per phase (qkv, o, w12, c, lm): this CTA's units [u0, u1), units per chunk, K
+    float qbias[kQkvBiasUnits][2];  // this layer's QKV bias pairs of the CTA's QKV units (loaded ahead)
     volatile int fail;  // a consumer wait expired
     int token;
     int last;
@@ -357,7 +359,8 @@ __device__ bool grid_sync(const DecodeArgs& a, Smem& s, uint32_t& nbar, int tid,
 // embedding) or flag-carrying words with `tag`.  Returns the CTA-wide failure
 // verdict (true = a wait expired somewhere in the CTA).
 __device__ bool load_norm(const DecodeArgs& a, const half* plain, const unsigned long long* ll, uint32_t tag,
-                          const half* w, Smem& s, int tid, uint32_t* xr, bool bad, int& np) {
+                          const half* w, Smem& s, int tid, uint32_t* xr, bool bad, int& np,
+                          float* stage_dst = nullptr, float stage_val = 0.f) {
     const uint4 wv = *reinterpret_cast<const uint4*>(w + tid * 8);  // in flight while polling
     uint4 v;
     if (plain) {
@@ -378,6 +381,7 @@ __device__ bool load_norm(const DecodeArgs& a, const half* plain, const unsigned
 #pragma unroll
     for (int e = 0; e < 8; ++e) of[e] = (xf[e] * r) * wf[e];
     *reinterpret_cast<uint4*>(s.xs + tid * 8) = pack8(of);
+    if (stage_dst) *stage_dst = stage_val;  // a value loaded before the poll, visible after the barrier
     named_bar_sync(1, 256);
     const int lane = tid & 31;
 #pragma unroll
@@ -468,10 +472,16 @@ __device__ __forceinline__ void gemv_phase(int PH, const DecodeArgs& a, Smem& s,
         float b0 = 0.f, b1 = 0.f;
         if (PH == PH_QKV) {
             if (ej >= 0) {
-                const int u = cu + ej, sec = u / (kHidden / 2), v = u % (kHidden / 2);
-                const int i1 = sec * kHidden + (v / 64) * kHeadDim + (v % 64);
-                b0 = h2f(c.bias[i1]);
-                b1 = h2f(c.bias[i1 + 64]);
+                const int u = cu + ej;
+                if (u1 - u0 <= kQkvBiasUnits) {  // staged by the QKV prologue
+                    b0 = s.qbias[u - u0][0];
+                    b1 = s.qbias[u - u0][1];
+                } else {
+                    const int sec = u / (kHidden / 2), v = u % (kHidden / 2);
+                    const int i1 = sec * kHidden + (v / 64) * kHeadDim + (v % 64);
+                    b0 = h2f(c.bias[i1]);
+                    b1 = h2f(c.bias[i1 + 64]);
+                }
             }
         }
         const half* buf = reinterpret_cast<const half*>(s.ring[warp]);
@@ -744,7 +754,20 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
                                      : ph == PH_LM ? tags(step, l, LL_XC)
                                                    : (l > 0 ? tags(step, l - 1, LL_XC) : 0u);
                 const half* w = ph == PH_QKV ? L.ln1 : ph == PH_W12 ? L.ln2 : a.lnf;
-                failed = load_norm(a, plain, src, tag, w, s, tid, xr, bad, np);
+                // QKV: thread i loads half (i & 1) of the bias pair of QKV unit u0 + i / 2 now;
+                // load_norm stores it into s.qbias once its poll is over
+                float* bdst = nullptr;
+                float bval = 0.f;
+                if (ph == PH_QKV) {
+                    const int u0 = s.range[0][0], nu = s.range[0][1] - u0;
+                    if (nu <= kQkvBiasUnits && tid < 2 * nu) {
+                        const int u = u0 + (tid >> 1), sec = u / (kHidden / 2), v = u % (kHidden / 2);
+                        const int i1 = sec * kHidden + (v / 64) * kHeadDim + (v % 64) + (tid & 1) * 64;
+                        bval = h2f(L.qkv_b[i1]);
+                        bdst = &s.qbias[tid >> 1][tid & 1];
+                    }
+                }
+                failed = load_norm(a, plain, src, tag, w, s, tid, xr, bad, np, bdst, bval);
                 if (failed) break;
             }
             c.tag = tags(step, l, ph == PH_QKV ? LL_QKV : ph == PH_O ? LL_XO : ph == PH_W12 ? LL_ACT : LL_XC);
@@ -824,6 +847,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
 
 }  // namespace
 
+static_assert(sizeof(Smem) <= 232448, "the decode kernel's shared memory exceeds the 227 KB opt-in limit");
 size_t decode_smem_bytes() { return sizeof(Smem); }
 
 // Number of flag tags one launch of n_steps consumes (the host advances its

@@ -14,7 +14,7 @@
 #include <algorithm>
 #include <mutex>
 
-#include "../../include/llmdiy_kernels.h"
+#include "llmdiy_kernels.h"
 #include "ops.cuh"
 
 using namespace llmdiy;
