@@ -58,6 +58,9 @@ int llmdiy_fd_opt_stage2(const uint16_t* Opart, const float* LSE, uint16_t* O, i
  * accumulation on the tcgen05 tensor cores (TMEM accumulators, TMA-staged 128x256x64 tiles), fp16 C.
  * K must be a multiple of 8 and the pointers 16-byte aligned. */
 int llmdiy_gemm_tc(const uint16_t* A, const uint16_t* W, uint16_t* C, int M, int N, int K, void* stream);
+/* As llmdiy_gemm_tc with B[K,N] row-major (the reference's transposed-weight layout; N a multiple of 64),
+ * staged as an MN-major tcgen05 operand. */
+int llmdiy_gemm_tc_kn(const uint16_t* A, const uint16_t* B, uint16_t* C, int M, int N, int K, void* stream);
 /* After synchronising: 0, or 1 if a tensor-core GEMM on this device had a pipeline wait expire since the
  * last call (its output is then not valid). */
 int llmdiy_gemm_tc_status(void);

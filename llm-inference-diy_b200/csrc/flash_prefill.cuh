@@ -9,6 +9,7 @@
 // accumulator fragments (scale 1/sqrt(128), __expf), P reused in registers as
 // the A operand of O += P V (V fragments by ldmatrix.trans).
 #pragma once
+#include "decode.h"
 #include "ops.cuh"
 
 namespace llmdiy {
@@ -57,7 +58,7 @@ LLMDIY_DEV uint32_t pack_h2(float lo, float hi) {
 
 // q: [n][ldq] rows of the prompt (head h at h*128); kc, vc: cache [rows][ldkv];
 // att: [n][ldq].  Grid (ceil(n/64), heads); the x index runs longest tiles first.
-__global__ void __launch_bounds__(kFpThreads) flash_prefill_k(const half* __restrict__ q, const half* __restrict__ kc,
+static __global__ void __launch_bounds__(kFpThreads) flash_prefill_k(const half* __restrict__ q, const half* __restrict__ kc,
                                                              const half* __restrict__ vc, half* __restrict__ att,
                                                              int n, int p0, int ldq, int ldkv) {
     extern __shared__ __align__(128) uint8_t fp_smem_raw[];

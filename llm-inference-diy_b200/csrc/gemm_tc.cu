@@ -53,6 +53,18 @@ bool make_kmajor_map(CUtensorMap* m, const void* base, int rows, int K, int ld, 
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_mnmajor_map(CUtensorMap* m, const void* base, int K, int N, int ld) {
+    EncodeTiled enc = encode_fn();
+    if (!enc || (reinterpret_cast<uintptr_t>(base) & 15) || (ld % 8) || K <= 0 || N <= 0) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)K};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)kGemmBK};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int* gemm_err_word() {
     static std::mutex mu;
     static int* words[64] = {};
@@ -84,3 +96,12 @@ extern "C" int llmdiy_gemm_tc(const uint16_t* A, const uint16_t* W, uint16_t* C,
 }
 
 extern "C" int llmdiy_gemm_tc_status(void) { return gemm_tc_status(); }
+
+// C[M,N] = A[M,K] * B[K,N] with B in the reference's transposed-weight layout (test entry for
+// the MN-major operand path; llmdiy_hgemm_swizzle_nn uses it).
+extern "C" int llmdiy_gemm_tc_kn(const uint16_t* A, const uint16_t* B, uint16_t* C, int M, int N, int K,
+                                 void* stream) {
+    PlainStore epi{reinterpret_cast<half*>(C), N, N};
+    return launch_gemm_tc_kn(reinterpret_cast<const half*>(A), K, reinterpret_cast<const half*>(B), N, M, N, K, epi,
+                             reinterpret_cast<cudaStream_t>(stream));
+}

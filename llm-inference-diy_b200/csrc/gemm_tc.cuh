@@ -38,7 +38,9 @@ struct GemmSmem {
 // The epilogue op receives, per thread, one output row and 16 consecutive
 // columns [n, n+16) of fp32 accumulators (already masked to n < N by the caller
 // only at whole-16 granularity: the op checks its own column bound).
-template <int BN, class Epi>
+// kBMN: B is stored [K][N] (N contiguous, the reference's transposed-weight layout) and staged
+// MN-major: per stage BN/64 TMA boxes of 64 N x 64 K rows, 8 KB apart.
+template <int BN, class Epi, bool kBMN = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_k(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, int M, int N, int K,
               Epi epi, int* err) {
@@ -82,11 +84,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             mbar_arrive_expect_tx(&s.full[st], kStageBytes);
             tma_load_2d(s.a[st], &tma, (kb0 + kb) * kGemmBK, m0, &s.full[st]);
-            tma_load_2d(s.b[st], &tmb, (kb0 + kb) * kGemmBK, n0, &s.full[st]);
+            if constexpr (kBMN) {
+#pragma unroll
+                for (int j = 0; j < BN / 64; ++j)
+                    tma_load_2d(s.b[st] + j * 64 * kGemmBK, &tmb, n0 + 64 * j, (kb0 + kb) * kGemmBK, &s.full[st]);
+            } else {
+                tma_load_2d(s.b[st], &tmb, (kb0 + kb) * kGemmBK, n0, &s.full[st]);
+            }
             ++issued;
         }
     } else if (warp == 1 && lane == 0) {
-        constexpr uint32_t idesc = umma_idesc_f16_f32(kGemmBM, BN);
+        constexpr uint32_t idesc = umma_idesc_f16_f32(kGemmBM, BN, kBMN);
         int kb = 0;
         for (; kb < KB; ++kb) {
             const int st = kb % kGemmStages;
@@ -97,9 +105,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tc_fence_after();
             const uint32_t a0 = smem_u32(s.a[st]), b0 = smem_u32(s.b[st]);
 #pragma unroll
-            for (int k = 0; k < kGemmBK / 16; ++k)
-                umma_f16(tmem, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc,
-                         (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < kGemmBK / 16; ++k) {
+                // K-major: 16 K-elements = 32 bytes within each 128-byte row; MN-major: 16 K-rows = 2 KB
+                const uint64_t bdesc = kBMN ? umma_desc_sw128_mn(b0 + 2048 * k, 64 * kGemmBK * 2, 1024)
+                                            : umma_desc_sw128(b0 + 32 * k);
+                umma_f16(tmem, umma_desc_sw128(a0 + 32 * k), bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
             umma_commit(&s.empty[st]);  // frees the stage once these MMAs have read it
         }
         umma_commit(&s.accum);  // all MMAs issued so far (a failed loop commits what it has)

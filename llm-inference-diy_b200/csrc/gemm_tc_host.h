@@ -13,6 +13,8 @@ namespace llmdiy {
 constexpr int kGemmBN = 256;  // output columns per CTA tile (UMMA N = 256)
 // K-major fp16 operand [rows][K] (row pitch ld elements), box 64 x box_rows, 128-byte swizzle.
 bool make_kmajor_map(CUtensorMap* m, const void* base, int rows, int K, int ld, int box_rows);
+// MN-major fp16 operand [K][N] (row pitch ld elements): box 64 N x 64 K rows, 128-byte swizzle.
+bool make_mnmajor_map(CUtensorMap* m, const void* base, int K, int N, int ld);
 int* gemm_err_word();  // per-device error word of the GEMM kernels (set when a wait expires)
 int gemm_tc_status();  // 0, or 1 once any GEMM of this device recorded an expired wait
 
@@ -38,6 +40,27 @@ int launch_gemm_tc(const half* A, int lda, const half* W, int ldw, int M, int N,
     const int per = (KB + ksplit - 1) / ksplit;
     if ((ksplit - 1) * per >= KB) return (int)cudaErrorInvalidValue;  // an empty slice
     dim3 grid((N + BN - 1) / BN, (M + kGemmBM - 1) / kGemmBM, ksplit);
+    kern<<<grid, kGemmThreads, sizeof(GemmSmem<BN>), st>>>(ta, tb, M, N, K, epi, err);
+    return (int)cudaGetLastError();
+}
+
+// C = A[M,K] * B[K,N] with B in the reference's [K,N] layout (MN-major operand).
+template <class Epi>
+int launch_gemm_tc_kn(const half* A, int lda, const half* B, int ldb, int M, int N, int K, const Epi& epi,
+                      cudaStream_t st) {
+    if (M <= 0 || N <= 0 || K <= 0 || (N % 64)) return (int)cudaErrorInvalidValue;
+    constexpr int BN = kGemmBN;
+    CUtensorMap ta, tb;
+    if (!make_kmajor_map(&ta, A, M, K, lda, kGemmBM) || !make_mnmajor_map(&tb, B, K, N, ldb))
+        return (int)cudaErrorInvalidValue;
+    int* err = gemm_err_word();
+    if (!err) return (int)cudaErrorMemoryAllocation;
+    auto kern = gemm_tc_k<BN, Epi, true>;
+    static std::once_flag attr;
+    std::call_once(attr, [&] {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(GemmSmem<BN>));
+    });
+    dim3 grid((N + BN - 1) / BN, (M + kGemmBM - 1) / kGemmBM, 1);
     kern<<<grid, kGemmThreads, sizeof(GemmSmem<BN>), st>>>(ta, tb, M, N, K, epi, err);
     return (int)cudaGetLastError();
 }

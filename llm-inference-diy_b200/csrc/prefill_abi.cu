@@ -4,8 +4,16 @@
 //
 // These are the op-level entry points for callers that hold row-major
 // [K,N] weights and per-head attention buffers, exactly as the reference's
-// prefill does.  They accumulate in fp32 (the reference accumulates the GEMM
-// and the attention scores in fp16).
+// prefill does: the GEMM runs on the tcgen05 tensor cores (B staged
+// MN-major), the attention on the flash-attention kernel of the engine's
+// prefill; both accumulate in fp32 (the reference accumulates the GEMM and
+// the attention scores in fp16).  Shapes the TMA path cannot take (N not a
+// multiple of 64, unaligned rows) use the CUDA-core kernels below.
+#include <mutex>
+
+#include "flash_prefill.cuh"
+#include "gemm_tc_host.h"
+#include "llmdiy_kernels.h"
 #include "ops.cuh"
 
 using namespace llmdiy;
@@ -13,6 +21,7 @@ using namespace llmdiy;
 namespace {
 
 inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // C[M,N] = A[M,K] * B[K,N], all row-major fp16, fp32 accumulation.
 // 64x64 output tile per CTA, 256 threads x (4x4) outputs, K staged 16 at a time.
@@ -56,37 +65,16 @@ __global__ void __launch_bounds__(256) gemm_rr_k(const half* __restrict__ A, con
         }
 }
 
-// Causal single-head attention, one warp per query row (keys 0..row),
-// rows of Q/O at stride_q and of K/V at stride_kv (halves).
-__global__ void __launch_bounds__(256) causal_attn_rows_k(const half* __restrict__ Q, const half* __restrict__ K,
-                                                           const half* __restrict__ V, half* __restrict__ O, int N,
-                                                           int stride_q, int stride_kv) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, dl = (lane & 15) * 8;
-    const int row = blockIdx.x * 8 + warp;
-    if (row >= N) return;
-    float q8[8];
-    unpack8(*reinterpret_cast<const uint4*>(Q + (size_t)row * stride_q + dl), q8);
-    const float scale = 1.0f / sqrtf(128.0f);
-    float m = -INFINITY, l = 0.f, o8[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) o8[e] = 0.f;
-    attend_rows<false>(K, V, stride_kv, 0, row + 1, q8, scale, m, l, o8);
-    combine_halfwarps(m, l, o8);
-    if (lane < 16) {
-        const float inv = __frcp_rn(l);
-        float of[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) of[e] = o8[e] * inv;
-        *reinterpret_cast<uint4*>(O + (size_t)row * stride_q + dl) = pack8(of);
-    }
-}
-
 }  // namespace
 
 extern "C" {
 
 int llmdiy_hgemm_swizzle_nn(uint16_t* A, uint16_t* B, uint16_t* C, int M, int N, int K, void* stream) {
     if (M <= 0 || N <= 0 || K <= 0) return (int)cudaErrorInvalidValue;
+    // tcgen05 path (B staged MN-major by TMA) where the layout allows it
+    if (N % 64 == 0 && K % 8 == 0 && aligned16(A) && aligned16(B) && aligned16(C))
+        return llmdiy_gemm_tc_kn(A, B, C, M, N, K, stream);
+    // any other shape: CUDA-core tiles
     dim3 grid((N + 63) / 64, (M + 63) / 64);
     gemm_rr_k<<<grid, 256, 0, S(stream)>>>(reinterpret_cast<const half*>(A), reinterpret_cast<const half*>(B),
                                            reinterpret_cast<half*>(C), M, N, K);
@@ -109,7 +97,14 @@ int llmdiy_flash_attn_tuned_A(uint16_t* Q, uint16_t* K, uint16_t* V, uint16_t* O
     // 16-byte vector accesses: every row start must be 16-byte aligned
     auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
     if (!al(q) || !al(k) || !al(v) || !al(o)) return (int)cudaErrorInvalidValue;
-    causal_attn_rows_k<<<(N + 7) / 8, 256, 0, S(stream)>>>(q, k, v, o, N, stride_Q, stride_KV);
+    // tensor-core flash attention (one head: grid.y = 1, head offset 0)
+    static std::once_flag attr;
+    std::call_once(attr, [] {
+        cudaFuncSetAttribute(flash_prefill_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(FlashPrefillSmem));
+    });
+    flash_prefill_k<<<dim3((N + kFpRows - 1) / kFpRows, 1), kFpThreads, sizeof(FlashPrefillSmem), S(stream)>>>(
+        q, k, v, o, N, 0, stride_Q, stride_KV);
     return (int)cudaGetLastError();
 }
 

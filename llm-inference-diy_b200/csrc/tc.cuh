@@ -35,12 +35,25 @@ LLMDIY_DEV uint64_t umma_desc_sw128(uint32_t addr) {
     d |= (uint64_t)2 << 61;             // SWIZZLE_128B
     return d;
 }
-// Instruction descriptor of kind::f16 with fp16 A and B (both K-major) and an
-// fp32 accumulator of M x N.
-__host__ __device__ constexpr uint32_t umma_idesc_f16_f32(int M, int N) {
+// Shared-memory matrix descriptor of an MN-major operand staged with 128-byte
+// swizzling: atoms of 64 MN-elements x 8 K-rows (1024 B); `lbo` = bytes
+// between atoms adjacent in MN, `sbo` = bytes between the 8-row K groups.
+LLMDIY_DEV uint64_t umma_desc_sw128_mn(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+// Instruction descriptor of kind::f16 with fp16 A (K-major) and B (K-major, or
+// MN-major when b_mn), fp32 accumulator of M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_f16_f32(int M, int N, bool b_mn = false) {
     return (1u << 4)                          // D format: f32
            | (0u << 7) | (0u << 10)           // A, B format: f16
-           | (0u << 15) | (0u << 16)          // A, B K-major
+           | (0u << 15)                       // A K-major
+           | ((b_mn ? 1u : 0u) << 16)         // B major-ness
            | ((uint32_t)(N >> 3) << 17)       // N / 8
            | ((uint32_t)(M >> 4) << 24);      // M / 16
 }

@@ -72,6 +72,7 @@ def lib() -> ctypes.CDLL:
         "llmdiy_fd_v5_split_stage1": [P, P, P, P, P, I, I, I, P],
         "llmdiy_fd_opt_stage2": [P, P, P, I, P],
         "llmdiy_gemm_tc": [P, P, P, I, I, I, P],
+        "llmdiy_gemm_tc_kn": [P, P, P, I, I, I, P],
         "llmdiy_gemm_tc_status": [],
         "llmdiy_fd_multihead": [P, P, P, P, I, I, I, P, SZ, P],
         "llmdiy_fd_mh_partials": [P, P, P, I, I, I, P, P, SZ, P],
@@ -193,6 +194,11 @@ def fd_opt_stage2(Opart, LSE, O, num_chunks, stream=None):
 def gemm_tc(A, W, C, M, N, K, stream=None):
     """C[M,N] = A[M,K] @ W[N,K]^T on the tcgen05 tensor cores (fp16 in/out, fp32 accumulation)."""
     _check(lib().llmdiy_gemm_tc(_p(A), _p(W), _p(C), M, N, K, _p(stream)), "gemm_tc")
+
+
+def gemm_tc_kn(A, B, C, M, N, K, stream=None):
+    """C[M,N] = A[M,K] @ B[K,N] (B in the reference's [K,N] layout) on the tcgen05 tensor cores."""
+    _check(lib().llmdiy_gemm_tc_kn(_p(A), _p(B), _p(C), M, N, K, _p(stream)), "gemm_tc_kn")
 
 
 def gemm_tc_status():

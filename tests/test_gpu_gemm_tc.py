@@ -25,6 +25,20 @@ def test_gemm_tc(rng, M, N, K):
     assert err.max() <= 0, (float(err.max()), np.unravel_index(err.argmax(), err.shape))
 
 
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (200, 384, 2048), (127, 5504, 2048), (64, 2048, 5504)])
+def test_gemm_tc_kn(rng, M, N, K):
+    """B in the reference's [K,N] layout (MN-major tcgen05 operand)."""
+    A = (rng.standard_normal((M, K)) * 0.5).astype(np.float16)
+    B = (rng.standard_normal((K, N)) * (1.0 / np.sqrt(K))).astype(np.float16)
+    dA, dB, C = dev(A), dev(B), zeros16(M * N)
+    L.gemm_tc_kn(dA.data_ptr(), dB.data_ptr(), C.data_ptr(), M, N, K)
+    got = host(C).reshape(M, N).astype(np.float64)
+    assert L.gemm_tc_status() == 0
+    exp = A.astype(np.float64) @ B.astype(np.float64)
+    err = np.abs(got - exp) - (np.abs(exp) * 2.0 ** -10 + 1e-3)
+    assert err.max() <= 0, (float(err.max()), np.unravel_index(err.argmax(), err.shape))
+
+
 def test_gemm_tc_rejects_bad_arguments():
     import torch
     x = torch.zeros(4096, dtype=torch.float16, device="cuda")

@@ -164,7 +164,7 @@ def test_fd_v5_split(oracle, rng, ref, L_, stride):
         assert max_abs(host(O), host(rO)) < 1e-3
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (127, 6144, 2048), (300, 200, 100)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (127, 6144, 2048), (300, 200, 100), (2048, 5504, 2048)])
 def test_hgemm_swizzle_nn(oracle, rng, M, N, K):
     A = refmath.h((rng.random((M, K)) - 0.5) * 0.1)
     B = refmath.h((rng.random((K, N)) - 0.5) * 0.1)
@@ -173,7 +173,7 @@ def test_hgemm_swizzle_nn(oracle, rng, M, N, K):
     assert max_abs(host(C).reshape(M, N), oracle.hgemm_kn(A, B)) < 2e-2
 
 
-@pytest.mark.parametrize("N", [1, 100, 257])
+@pytest.mark.parametrize("N", [1, 100, 257, 1000])
 def test_flash_attn_causal(oracle, rng, ref, N):
     Q = refmath.h(rng.standard_normal(N * 128))
     K = refmath.h(rng.standard_normal(N * 128))
