@@ -197,3 +197,27 @@ def test_reference_engine_stream(small_bin, engine):
     n_same = next((i for i, (a, b) in enumerate(zip(ours, ref)) if a != b), min(len(ours), len(ref)))
     # one-token prompt: the reference runs only its decode path (no fp16-accumulating prefill)
     assert n_same >= min(64, len(ref)), (n_same, ours[:70], ref[:70])
+
+
+def test_chunked_prefill_matches_oracle():
+    """A prompt longer than the prefill's 2048-row chunk: the second chunk attends over the first
+    chunk's cached rows.  KV rows of the last layer across the chunk boundary against the oracle."""
+    import oracle as orc
+    cfg = dict(SMALL, max_seqlen=2200)
+    d = tempfile.mkdtemp()
+    p = os.path.join(d, "chunk.bin")
+    L.write_random_bin(p, L.make_config(**cfg), seed=SEED + 1)
+    e = L.Engine(p)
+    m = orc.OracleModel(p, nthreads=os.cpu_count() or 8)
+    rng = np.random.default_rng(21)
+    prompt = rng.integers(0, cfg["vocab_size"], 2100).tolist()
+    e.prefill(prompt)
+    m.prefill(prompt)
+    for lo, n in ((0, 16), (2040, 60)):
+        k, v = e.kv(1, lo, n)
+        ok_, ov = m.kv(1, lo, n)
+        assert float(np.max(np.abs(k.astype(np.float32) - ok_.astype(np.float32)))) < 2e-2, lo
+        assert float(np.max(np.abs(v.astype(np.float32) - ov.astype(np.float32)))) < 2e-2, lo
+    e.close()
+    m.close()
+    os.remove(p)
