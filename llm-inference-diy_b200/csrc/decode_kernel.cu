@@ -374,7 +374,7 @@ __device__ bool load_norm(const DecodeArgs& a, const half* plain, const unsigned
     if (named_bar_or(1, 256, bad)) return true;
     probe(a, tid, np);
     *reinterpret_cast<uint4*>(s.xraw + tid * 8) = v;
-    const float r = rms_scale_tree256(s.xraw, kHidden, 1e-6f, s.red, tid, 1);
+    const float r = rms_scale_regs2048(v, 1e-6f, s.red, tid, 1);  // v = this thread's eight elements
     float xf[8], wf[8], of[8];
     unpack8(v, xf);
     unpack8(wv, wf);
@@ -468,7 +468,21 @@ __device__ __forceinline__ void gemv_phase(int PH, const DecodeArgs& a, Smem& s,
         const unsigned long long t1 = a.prof_prod ? (unsigned long long)clock64() : 0ull;
         // the unit whose epilogue this lane runs: lane 8j after dot6_regs, lane j after dot2_smem
         const int ej = PH == PH_C ? (lane < nun ? lane : -1) : (((lane & 7) == 0 && (lane >> 3) < nun) ? lane >> 3 : -1);
-        // QKV: the bias pair of that unit is fetched before the dot products
+        const half* buf = reinterpret_cast<const half*>(s.ring[warp]);
+        float r0s = 0.f, r1s = 0.f;  // the epilogue lane's two dot products
+        if (PH == PH_C) {
+#pragma unroll 1
+            for (int j = 0; j < nun; ++j) {
+                const half* r0 = buf + (size_t)j * 2 * K;
+                float s0, s1;
+                dot2_smem(r0, r0 + K, s.act, K, lane, s0, s1);
+                if (lane == j) { r0s = s0; r1s = s1; }
+            }
+        } else {
+            dot6_regs(buf, xr, lane, r0s, r1s);
+        }
+        // QKV: the bias pair of that unit, read after the dot products (read
+        // before them, it put about 1.5 us per layer on the critical path)
         float b0 = 0.f, b1 = 0.f;
         if (PH == PH_QKV) {
             if (ej >= 0) {
@@ -483,19 +497,6 @@ __device__ __forceinline__ void gemv_phase(int PH, const DecodeArgs& a, Smem& s,
                     b1 = h2f(c.bias[i1 + 64]);
                 }
             }
-        }
-        const half* buf = reinterpret_cast<const half*>(s.ring[warp]);
-        float r0s = 0.f, r1s = 0.f;  // the epilogue lane's two dot products
-        if (PH == PH_C) {
-#pragma unroll 1
-            for (int j = 0; j < nun; ++j) {
-                const half* r0 = buf + (size_t)j * 2 * K;
-                float s0, s1;
-                dot2_smem(r0, r0 + K, s.act, K, lane, s0, s1);
-                if (lane == j) { r0s = s0; r1s = s1; }
-            }
-        } else {
-            dot6_regs(buf, xr, lane, r0s, r1s);
         }
         if (ej >= 0) epilogue(PH, a, s, c, cu + ej, r0s, r1s, b0, b1);
         __syncwarp();
@@ -548,11 +549,75 @@ __device__ void prefetch_critical(const DecodeArgs& a, const Smem& s, const Step
     }
 }
 
-// Split-KV attention of one (head, split) per CTA; the last CTA to finish a
-// head merges the 9 partials and publishes att for that head.  Rows < pos
-// come from the KV cache (written by earlier steps, ordered by the step
-// barrier); the query and the new row pos come from the QKV phase's words.
-// Returns the CTA-wide failure verdict.
+// Cached rows of one warp's attention share: half-warp hw takes rows
+// w0 + 2j + hw (j < 4) of [w0, w1); lane (l & 15) holds dims 8(l & 15) ..
+// +7 of each.  Loads past w1 are skipped (zero registers).  The rows were
+// written by earlier steps (ordered by the step barrier) and prefetched to L2
+// at the start of the layer; .cg keeps them out of the non-coherent L1.
+__device__ __forceinline__ void kv_rows_load(const half* K, const half* V, int w0, int w1, int lane, uint4* kr,
+                                             uint4* vr) {
+    const int hw = lane >> 4, dl = (lane & 15) * 8;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int r = w0 + 2 * j + hw;
+        kr[j] = vr[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (r < w1) {
+            kr[j] = ld_cg_u4(K + (size_t)r * kHidden + dl);
+            vr[j] = ld_cg_u4(V + (size_t)r * kHidden + dl);
+        }
+    }
+}
+
+// Fold the (up to 8) rows loaded by kv_rows_load into the half-warp's
+// online-softmax state (m over scaled scores, l, unnormalised o8).  w0 and
+// w1 are warp-uniform, so every shuffle runs with all 32 lanes.
+__device__ __forceinline__ void kv_rows_fold(const uint4* kr, const uint4* vr, int w0, int w1, int lane,
+                                             const float* q8, float scale, float& m, float& l, float* o8) {
+    const int hw = lane >> 4;
+    float sc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float kf[8];
+        unpack8(kr[j], kf);
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d = __fmaf_rn(q8[e], kf[e], d);
+        sc[j] = d;
+    }
+#pragma unroll
+    for (int mk = 8; mk >= 1; mk >>= 1)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], mk);
+    float mx = m;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        sc[j] = (w0 + 2 * j + hw < w1) ? sc[j] * scale : -INFINITY;
+        mx = fmaxf(mx, sc[j]);
+    }
+    if (mx == -INFINITY) return;  // no row for this half-warp yet
+    const float corr = (m == -INFINITY) ? 0.f : __expf(m - mx);
+    l *= corr;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o8[e] *= corr;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float p = sc[j] == -INFINITY ? 0.f : __expf(sc[j] - mx);
+        l += p;
+        float vf[8];
+        unpack8(vr[j], vf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o8[e] = __fmaf_rn(p, vf[e], o8[e]);
+    }
+    m = mx;
+}
+
+// Split-KV attention of one (head, split) per CTA (qwen_infer.cu:646-677 with
+// the reference's flash-decoding split, kernels/flash_decoding.cuh): the
+// CTA's rows < pos come from the KV cache, the query and row pos from the
+// QKV phase's words.  Each warp folds its cached rows eight at a time (one
+// L2 round trip per eight rows).  Splits 1..8 publish (o, m, l) partials as
+// flag words; split 0 merges them in split order and publishes att for the
+// head.  Returns the CTA-wide failure verdict.
 __device__ bool attention_phase(const DecodeArgs& a, Smem& s, const StepCtx& c, const Tags& tags, int tid,
                                 bool bad) {
     const int b = blockIdx.x;
@@ -562,6 +627,12 @@ __device__ bool attention_phase(const DecodeArgs& a, Smem& s, const StepCtx& c, 
     const int warp = tid >> 5, lane = tid & 31, dl = (lane & 15) * 8;
     const int r0 = (int)((long long)L * sp / S), r1 = (int)((long long)L * (sp + 1) / S);
     const bool has_new = active && r0 < L && r1 == L;  // this split owns row pos
+    const int rend = has_new ? L - 1 : r1;             // rows from the cache
+    const int n = active ? rend - r0 : 0;
+    const int w0 = r0 + n * warp / 8, w1 = r0 + n * (warp + 1) / 8;
+    const half* K = c.kcl + h * kHeadDim;
+    const half* V = c.vcl + h * kHeadDim;
+    uint4 kr[4], vr[4];
     const uint32_t tq = tags(c.step, c.layer, LL_QKV);
     float q8[8], m = -INFINITY, l = 0.f, o8[8];
 #pragma unroll
@@ -579,11 +650,12 @@ __device__ bool attention_phase(const DecodeArgs& a, Smem& s, const StepCtx& c, 
     if (active) {
         unpack8(*reinterpret_cast<const uint4*>(&s.qkv_new[0][dl]), q8);
         const float scale = __frcp_rn(sqrtf((float)kHeadDim));
-        const int rend = has_new ? L - 1 : r1;  // rows from the cache
-        const int n = rend - r0;
-        const int w0 = r0 + n * warp / 8, w1 = r0 + n * (warp + 1) / 8;
-        if (w0 < w1)
-            attend_rows<true>(c.kcl + h * kHeadDim, c.vcl + h * kHeadDim, kHidden, w0, w1, q8, scale, m, l, o8);
+#pragma unroll 1
+        for (int r = w0; r < w1; r += 8) {
+            const int re = w1 < r + 8 ? w1 : r + 8;
+            kv_rows_load(K, V, r, re, lane, kr, vr);
+            kv_rows_fold(kr, vr, r, re, lane, q8, scale, m, l, o8);
+        }
         combine_halfwarps(m, l, o8);
         if (has_new && warp == 0) {
             // row pos from the QKV phase's words
@@ -640,12 +712,12 @@ __device__ bool attention_phase(const DecodeArgs& a, Smem& s, const StepCtx& c, 
     static_assert(kAttnSplits - 1 <= kConsumerWarps, "one shared row per other split");
     {
         constexpr int kWords = (S - 1) * 130, kPer = (kWords + kDecodeThreads - 1) / kDecodeThreads;
-        const int n = (kWords - tid + kDecodeThreads - 1) / kDecodeThreads;
+        const int nw = (kWords - tid + kDecodeThreads - 1) / kDecodeThreads;
         uint32_t d[kPer];
-        bad |= !ll_read_n<kPer>(part + 130 + tid, kDecodeThreads, n, tp, d);
+        bad |= !ll_read_n<kPer>(part + 130 + tid, kDecodeThreads, nw, tp, d);
 #pragma unroll
         for (int k = 0; k < kPer; ++k) {
-            if (k >= n) break;
+            if (k >= nw) break;
             const int i = tid + k * kDecodeThreads, j = i / 130, e = i % 130;
             const float v = __uint_as_float(d[k]);
             if (e < kHeadDim) s.so[j][e] = v;

@@ -57,6 +57,53 @@ LLMDIY_DEV float rms_scale_tree256(const half* x, int d, float eps, float* red, 
     return red[16];
 }
 
+// rms_scale_tree256 for d = 2048 with each thread's own eight elements
+// (x[8*tid .. 8*tid+7], fp16 pairs in v) already in registers: the same
+// summation tree without reading the vector back from memory.
+LLMDIY_DEV float rms_scale_regs2048(const uint4& v, float eps, float* red, int tid, int bar_id) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        p0 = __fmaf_rn(f.x, f.x, p0);
+        p0 = __fmaf_rn(f.y, f.y, p0);
+    }
+#pragma unroll
+    for (int i = 2; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        p1 = __fmaf_rn(f.x, f.x, p1);
+        p1 = __fmaf_rn(f.y, f.y, p1);
+    }
+#pragma unroll
+    for (int m = 8; m >= 1; m >>= 1) {
+        p0 += __shfl_xor_sync(0xffffffffu, p0, m);
+        p1 += __shfl_xor_sync(0xffffffffu, p1, m);
+    }
+    float s = p0 + p1;
+    const int lane = tid & 31, warp = tid >> 5;
+    if (lane == 0) red[2 * warp] = s;
+    if (lane == 16) red[2 * warp + 1] = s;
+    named_bar_sync(bar_id, 256);
+    if (tid == 0) {
+        float t[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) t[j] = red[j] + 0.0f;
+#pragma unroll
+        for (int m = 8; m >= 1; m >>= 1) {
+            float u[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) u[j] = t[j] + t[j ^ m];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) t[j] = u[j];
+        }
+        float var = __fdividef(t[0], 2048.0f);
+        red[16] = rsqrtf(var + eps);
+    }
+    named_bar_sync(bar_id, 256);
+    return red[16];
+}
+
 // Online-softmax state of one attention partial: running max m (over scaled
 // scores), running sum l, unnormalised output o.
 struct SoftmaxState {
