@@ -531,19 +531,23 @@ __device__ __forceinline__ void prefetch_l2_line(const void* p) {
 // the KV cache for the attention phase (rows before pos, written by earlier
 // steps).  With HBM saturated by the weight stream, a demand miss on these
 // would cost several microseconds on the critical path.
-__device__ void prefetch_critical(const DecodeArgs& a, const Smem& s, const StepCtx& c, int l, int tid) {
+__device__ void prefetch_norms(const DecodeArgs& a, const Smem& s, int l, int tid) {
     const LayerPtrs& N = s.layers[l + 1 < a.NL ? l + 1 : 0];
     if (tid < 32) prefetch_l2_line(N.ln1 + tid * 64);
     else if (tid < 64) prefetch_l2_line(N.ln2 + (tid - 32) * 64);
     else if (tid < 160) prefetch_l2_line(N.qkv_b + (tid - 64) * 64);
     else if (tid < 192 && l + 1 == a.NL) prefetch_l2_line(a.lnf + (tid - 160) * 64);
+}
+__device__ void prefetch_kv_rows(const DecodeArgs& a, int l, int pos, int tid) {
     const int b = blockIdx.x;
     if (b < kHeads * kAttnSplits) {
-        const int h = b / kAttnSplits, sp = b % kAttnSplits, L = c.pos + 1;
+        const half* kcl = a.kc + (size_t)l * a.max_seqlen * kHidden;
+        const half* vcl = a.vc + (size_t)l * a.max_seqlen * kHidden;
+        const int h = b / kAttnSplits, sp = b % kAttnSplits, L = pos + 1;
         const int r0 = (int)((long long)L * sp / kAttnSplits), r1 = (int)((long long)L * (sp + 1) / kAttnSplits);
         const int rend = (r1 == L) ? L - 1 : r1;
         for (int i = tid; i < (rend - r0) * 4; i += kDecodeThreads) {
-            const half* base = ((i & 2) ? c.vcl : c.kcl) + (size_t)(r0 + (i >> 2)) * kHidden + h * kHeadDim;
+            const half* base = ((i & 2) ? vcl : kcl) + (size_t)(r0 + (i >> 2)) * kHidden + h * kHeadDim;
             prefetch_l2_line(base + (i & 1) * 64);
         }
     }
@@ -788,7 +792,8 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
                 c.kcl = a.kc + (size_t)l * a.max_seqlen * kHidden;
                 c.vcl = a.vc + (size_t)l * a.max_seqlen * kHidden;
                 c.bias = L.qkv_b;
-                prefetch_critical(a, s, c, l, tid);
+                prefetch_norms(a, s, l, tid);
+                if (l == 0) prefetch_kv_rows(a, 0, c.pos, tid);
             }
             probe(a, tid, np);
             if (ph == PH_O) {
@@ -812,6 +817,7 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
                 // SwiGLU output into s.act.  s.act was last read by the previous
                 // layer's C phase, which every warp has left (several named
                 // barriers since), so the words go straight to shared memory.
+                if (l + 1 < a.NL) prefetch_kv_rows(a, l + 1, c.pos, tid);
                 const int n = (a.IM - tid + kDecodeThreads - 1) / kDecodeThreads;
                 bad |= !ll_gather_act(a.ll_act + tid, n, tags(step, l, LL_ACT), s.act + tid);
                 failed = named_bar_or(1, 256, bad);

@@ -57,9 +57,13 @@ LLMDIY_DEV float rms_scale_tree256(const half* x, int d, float eps, float* red, 
     return red[16];
 }
 
-// rms_scale_tree256 for d = 2048 with each thread's own eight elements
-// (x[8*tid .. 8*tid+7], fp16 pairs in v) already in registers: the same
-// summation tree without reading the vector back from memory.
+// rms_scale_tree256 for d = 2048 (same summation tree, same bits) with each
+// thread's own eight elements (x[8*tid .. 8*tid+7], fp16 pairs in v) already
+// in registers, and one barrier: after the per-warp stage every warp replays
+// the final 16-value tree itself (lane j holds warp-sum j; the xor butterfly
+// computes t[j] + t[j^m] exactly as the serial replay does) and takes lane
+// 0's total.  `red` (>= 16 floats of shared memory) must not be rewritten
+// before every warp has read it (the caller's next barrier orders that).
 LLMDIY_DEV float rms_scale_regs2048(const uint4& v, float eps, float* red, int tid, int bar_id) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     float p0 = 0.f, p1 = 0.f;
@@ -80,28 +84,16 @@ LLMDIY_DEV float rms_scale_regs2048(const uint4& v, float eps, float* red, int t
         p0 += __shfl_xor_sync(0xffffffffu, p0, m);
         p1 += __shfl_xor_sync(0xffffffffu, p1, m);
     }
-    float s = p0 + p1;
+    const float s = p0 + p1;
     const int lane = tid & 31, warp = tid >> 5;
     if (lane == 0) red[2 * warp] = s;
     if (lane == 16) red[2 * warp + 1] = s;
     named_bar_sync(bar_id, 256);
-    if (tid == 0) {
-        float t[16];
+    float t = lane < 16 ? red[lane] + 0.0f : 0.f;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) t[j] = red[j] + 0.0f;
-#pragma unroll
-        for (int m = 8; m >= 1; m >>= 1) {
-            float u[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) u[j] = t[j] + t[j ^ m];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) t[j] = u[j];
-        }
-        float var = __fdividef(t[0], 2048.0f);
-        red[16] = rsqrtf(var + eps);
-    }
-    named_bar_sync(bar_id, 256);
-    return red[16];
+    for (int m = 8; m >= 1; m >>= 1) t = t + __shfl_xor_sync(0xffffffffu, t, m);
+    const float total = __shfl_sync(0xffffffffu, t, 0);
+    return rsqrtf(__fdividef(total, 2048.0f) + eps);
 }
 
 // Online-softmax state of one attention partial: running max m (over scaled
