@@ -44,6 +44,12 @@ typedef void (*llmdiy_token_cb)(int token, void* user);
 
 /* ---- QWDF file tooling ---- */
 int llmdiy_qwdf_read_config(const char* path, llmdiy_config* out);
+/* Check a .bin against the format (convert_weights.py:107-185 writes it, qwen_infer.cu:117-242 reads it):
+ * the magic, a non-zero config, a length covering every tensor, every fp16 value finite, and then
+ * whether the engine runs the config.  Returns 0 (valid), LLMDIY_ERR_FILE, LLMDIY_ERR_FORMAT or
+ * LLMDIY_ERR_UNSUPPORTED; the header goes to *cfg, the count of non-finite values to *nonfinite
+ * and a one-line verdict to msg (either pointer may be NULL). */
+int llmdiy_qwdf_validate(const char* path, llmdiy_config* cfg, uint64_t* nonfinite, char* msg, size_t msg_len);
 /* Seeded random weights: matrices, biases and wte ~ N(0, std_dev), RMSNorm weights = 1. */
 int llmdiy_qwdf_write_random(const char* path, const llmdiy_config* cfg, uint64_t seed, float std_dev, int nthreads);
 /* Elements [first, first+n) of tensor `tensor_id` (file order) of that random source, as fp16 bits. */

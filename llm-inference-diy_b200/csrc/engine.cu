@@ -119,14 +119,8 @@ int cuda_fail(llmdiy_engine* e, cudaError_t c, const char* what) {
     } while (0)
 
 int check_config(llmdiy_engine* e, const llmdiy_config& c) {
-    if (c.hidden_size != (uint32_t)kHidden || c.num_heads != (uint32_t)kHeads)
-        return fail(e, LLMDIY_ERR_UNSUPPORTED, "fused decode kernel is built for hidden_size 2048 / 16 heads x 128");
-    if (c.intermediate_size == 0 || c.intermediate_size % 32 || c.intermediate_size > 6144)
-        return fail(e, LLMDIY_ERR_UNSUPPORTED, "intermediate_size must be a multiple of 32 and <= 6144");
-    if (c.num_layers > (uint32_t)kMaxLayers)
-        return fail(e, LLMDIY_ERR_UNSUPPORTED, "at most 64 layers");
-    if (c.vocab_size == 0 || c.vocab_size % 2 || c.num_layers == 0 || c.max_seqlen == 0)
-        return fail(e, LLMDIY_ERR_UNSUPPORTED, "vocab_size must be even; layers and max_seqlen non-zero");
+    static_assert(kHidden == 2048 && kHeads == 16 && kMaxLayers == 64, "qwdf_unsupported states these limits");
+    if (const char* why = qwdf_unsupported(c)) return fail(e, LLMDIY_ERR_UNSUPPORTED, why);
     return LLMDIY_OK;
 }
 

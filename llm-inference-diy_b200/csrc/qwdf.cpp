@@ -31,6 +31,27 @@ TensorDesc qwdf_tensor(const llmdiy_config& c, int id) {
     }
 }
 
+const char* qwdf_unsupported(const llmdiy_config& c) {
+    if (c.hidden_size != 2048u || c.num_heads != 16u)
+        return "fused decode kernel is built for hidden_size 2048 / 16 heads x 128";
+    if (c.intermediate_size == 0 || c.intermediate_size % 32 || c.intermediate_size > 6144)
+        return "intermediate_size must be a multiple of 32 and <= 6144";
+    if (c.num_layers > 64u) return "at most 64 layers";
+    if (c.vocab_size == 0 || c.vocab_size % 2 || c.num_layers == 0 || c.max_seqlen == 0)
+        return "vocab_size must be even; layers and max_seqlen non-zero";
+    return nullptr;
+}
+
+void qwdf_tensor_name(const llmdiy_config& c, int id, char* out, size_t len) {
+    static const char* kLayer[T_PER_LAYER] = {"ln_1", "qkv_w", "qkv_b", "attn_proj_w", "ln_2", "ffn_w1", "ffn_w2",
+                                              "ffn_proj_w"};
+    const int last = qwdf_num_tensors(c) - 1;
+    if (id == 0) std::snprintf(out, len, "wte");
+    else if (id == last) std::snprintf(out, len, "lm_head");
+    else if (id == last - 1) std::snprintf(out, len, "ln_f");
+    else std::snprintf(out, len, "layer %d %s", (id - 1) / T_PER_LAYER, kLayer[(id - 1) % T_PER_LAYER]);
+}
+
 size_t qwdf_file_bytes(const llmdiy_config& c) {
     size_t n = sizeof(QwdfHeader);
     for (int i = 0; i < qwdf_num_tensors(c); ++i) {
@@ -128,6 +149,81 @@ int llmdiy_qwdf_read_config(const char* path, llmdiy_config* out) {
         h.intermediate_size == 0)
         return LLMDIY_ERR_FORMAT;
     if ((unsigned long long)size < (unsigned long long)qwdf_file_bytes(*out)) return LLMDIY_ERR_FORMAT;
+    return LLMDIY_OK;
+}
+
+int llmdiy_qwdf_validate(const char* path, llmdiy_config* cfg, uint64_t* nonfinite, char* msg, size_t msg_len) {
+    char scratch[8];
+    if (!msg || msg_len == 0) { msg = scratch; msg_len = sizeof(scratch); }
+    msg[0] = '\0';
+    if (nonfinite) *nonfinite = 0;
+    FILE* f = std::fopen(path, "rb");
+    if (!f) {
+        std::snprintf(msg, msg_len, "cannot open %s", path);
+        return LLMDIY_ERR_FILE;
+    }
+    QwdfHeader h{};
+    const size_t got = std::fread(&h, 1, sizeof(h), f);
+    if (got != sizeof(h) || h.magic != kQwdfMagic) {
+        std::fclose(f);
+        std::snprintf(msg, msg_len, "not a QWDF file (magic 0x%08x, expected 0x%08x)", h.magic, kQwdfMagic);
+        return LLMDIY_ERR_FORMAT;
+    }
+    const llmdiy_config c{h.vocab_size, h.hidden_size, h.num_layers, h.num_heads, h.intermediate_size, h.max_seqlen};
+    if (cfg) *cfg = c;
+    if (!c.vocab_size || !c.hidden_size || !c.num_layers || !c.num_heads || !c.intermediate_size) {
+        std::fclose(f);
+        std::snprintf(msg, msg_len, "header has a zero dimension");
+        return LLMDIY_ERR_FORMAT;
+    }
+    std::fseek(f, 0, SEEK_END);
+    const unsigned long long size = (unsigned long long)std::ftell(f);
+    const unsigned long long want = qwdf_file_bytes(c);
+    if (size < want) {
+        std::fclose(f);
+        std::snprintf(msg, msg_len, "truncated: %llu bytes, the header's config needs %llu", size, want);
+        return LLMDIY_ERR_FORMAT;
+    }
+    // every fp16 value finite (exponent bits not all ones), counted per tensor
+    std::fseek(f, (long)sizeof(QwdfHeader), SEEK_SET);
+    const size_t chunk = (size_t)1 << 22;
+    std::vector<uint16_t> buf(chunk);
+    uint64_t bad_total = 0;
+    int first_bad = -1;
+    uint64_t first_bad_count = 0;
+    for (int id = 0; id < qwdf_num_tensors(c); ++id) {
+        const TensorDesc d = qwdf_tensor(c, id);
+        const size_t n = d.rows * d.cols;
+        uint64_t bad = 0;
+        for (size_t i = 0; i < n; i += chunk) {
+            const size_t m = n - i < chunk ? n - i : chunk;
+            if (std::fread(buf.data(), 2, m, f) != m) {
+                std::fclose(f);
+                std::snprintf(msg, msg_len, "read error in tensor %d", id);
+                return LLMDIY_ERR_FILE;
+            }
+            for (size_t k = 0; k < m; ++k) bad += (buf[k] & 0x7C00u) == 0x7C00u;
+        }
+        if (bad && first_bad < 0) { first_bad = id; first_bad_count = bad; }
+        bad_total += bad;
+    }
+    std::fclose(f);
+    if (nonfinite) *nonfinite = bad_total;
+    if (bad_total) {
+        char name[64];
+        qwdf_tensor_name(c, first_bad, name, sizeof(name));
+        std::snprintf(msg, msg_len, "%llu non-finite fp16 values (first in %s: %llu)", (unsigned long long)bad_total,
+                      name, (unsigned long long)first_bad_count);
+        return LLMDIY_ERR_FORMAT;
+    }
+    if (const char* why = qwdf_unsupported(c)) {
+        std::snprintf(msg, msg_len, "valid QWDF file, not supported by the engine: %s", why);
+        return LLMDIY_ERR_UNSUPPORTED;
+    }
+    if (size > want)
+        std::snprintf(msg, msg_len, "valid; %llu trailing bytes after lm_head are ignored", size - want);
+    else
+        std::snprintf(msg, msg_len, "valid");
     return LLMDIY_OK;
 }
 

@@ -31,6 +31,14 @@ int qwdf_num_tensors(const llmdiy_config& c);
 TensorDesc qwdf_tensor(const llmdiy_config& c, int id);
 size_t qwdf_file_bytes(const llmdiy_config& c);
 
+// Nullptr when the engine's kernels run this config, else why not (the
+// decode kernel is built for hidden 2048 = 16 heads x 128, intermediate a
+// multiple of 32 up to 6144, at most 64 layers, an even vocabulary).
+const char* qwdf_unsupported(const llmdiy_config& c);
+
+// Name of tensor `id` in file order ("wte", "layer 3 qkv_w", ..., "lm_head").
+void qwdf_tensor_name(const llmdiy_config& c, int id, char* out, size_t len);
+
 // Fill n consecutive elements [first, first+n) of tensor `id` with the
 // seeded values (fp16 bits): N(0, std) from a counter-based Box-Muller
 // stream, or 1.0 for RMSNorm weights.

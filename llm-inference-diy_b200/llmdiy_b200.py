@@ -23,6 +23,7 @@ DRIVER_PATH = os.path.join(_HERE, "_build", "qwen_infer_b200")
 INCLUDE_DIR = os.path.join(os.path.dirname(_HERE), "include")
 
 STOP_IDS = (151645, 151643)  # qwen_infer.cu:808
+ERR_ARG, ERR_FILE, ERR_FORMAT, ERR_UNSUPPORTED, ERR_DEVICE, ERR_NOMEM = -1, -2, -3, -4, -5, -6  # llmdiy_engine.h
 
 
 class LlmdiyError(RuntimeError):
@@ -88,6 +89,7 @@ def lib() -> ctypes.CDLL:
         "llmdiy_transpose_weight": [P, P, I, I, P],
         "llmdiy_transpose_weight_gpu": [ctypes.POINTER(ctypes.c_void_p), I, I],
         "llmdiy_qwdf_read_config": [ctypes.c_char_p, ctypes.POINTER(Config)],
+        "llmdiy_qwdf_validate": [ctypes.c_char_p, ctypes.POINTER(Config), ctypes.POINTER(U64), ctypes.c_char_p, SZ],
         "llmdiy_qwdf_write_random": [ctypes.c_char_p, ctypes.POINTER(Config), U64, F, I],
         "llmdiy_qwdf_fill_tensor": [ctypes.POINTER(Config), I, U64, F, SZ, SZ, P, I],
         "llmdiy_engine_create": [ctypes.c_char_p, I, ctypes.POINTER(P)],
@@ -273,6 +275,18 @@ def read_bin_config(path: str) -> Config:
     return c
 
 
+def validate_bin(path: str) -> dict:
+    """Check a .bin against the QWDF format (llmdiy_qwdf_validate): {"status": 0 | LLMDIY_ERR_*,
+    "ok": bool, "config": dict or None, "nonfinite": int, "message": str}.  Never raises on a bad file."""
+    c = Config()
+    bad = ctypes.c_uint64(0)
+    msg = ctypes.create_string_buffer(512)
+    rc = lib().llmdiy_qwdf_validate(path.encode(), ctypes.byref(c), ctypes.byref(bad), msg, len(msg))
+    has_header = rc in (ERR_FORMAT, ERR_UNSUPPORTED, 0) and c.vocab_size != 0
+    return {"status": rc, "ok": rc == 0, "config": c.as_dict() if has_header else None,
+            "nonfinite": int(bad.value), "message": msg.value.decode()}
+
+
 def fill_tensor(cfg: Config, tensor_id: int, seed: int, first: int, n: int, std_dev: float = 0.02, nthreads=8):
     import numpy as np
     out = np.empty(n, dtype=np.uint16)
@@ -446,3 +460,36 @@ class Batch:
         self._chk(lib().llmdiy_batch_copy_kv(self._h, seq, layer, pos0, n, k.ctypes.data_as(ctypes.c_void_p),
                                              v.ctypes.data_as(ctypes.c_void_p)), "batch kv")
         return k.view(np.float16).reshape(n, H), v.view(np.float16).reshape(n, H)
+
+
+def _main(argv=None) -> int:
+    """QWDF file tooling: `validate FILE` checks a .bin (exit 0 when the engine can run it);
+    `write-random FILE [--layers N] [--vocab V] [--intermediate I] [--max-seqlen S] [--seed K]` writes
+    seeded random weights (N(0, 0.02), RMSNorm weights 1) in the same format."""
+    import argparse
+    import json
+    ap = argparse.ArgumentParser(prog="llmdiy_b200", description=_main.__doc__)
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    v = sub.add_parser("validate")
+    v.add_argument("file")
+    w = sub.add_parser("write-random")
+    w.add_argument("file")
+    w.add_argument("--layers", type=int, default=QWEN_1_8B["num_layers"])
+    w.add_argument("--vocab", type=int, default=QWEN_1_8B["vocab_size"])
+    w.add_argument("--intermediate", type=int, default=QWEN_1_8B["intermediate_size"])
+    w.add_argument("--max-seqlen", type=int, default=2048)
+    w.add_argument("--seed", type=int, default=0)
+    a = ap.parse_args(argv)
+    if a.cmd == "validate":
+        r = validate_bin(a.file)
+        print(json.dumps(r))
+        return 0 if r["ok"] else 1
+    cfg = make_config(vocab_size=a.vocab, num_layers=a.layers, intermediate_size=a.intermediate,
+                      max_seqlen=a.max_seqlen)
+    write_random_bin(a.file, cfg, seed=a.seed, nthreads=os.cpu_count() or 8)
+    print(json.dumps({"written": a.file, "config": cfg.as_dict()}))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(_main())

@@ -78,6 +78,65 @@ def test_qwdf_rejects_bad_files():
         L.read_bin_config(os.path.join(d, "missing.bin"))
 
 
+def test_qwdf_validate_verdicts():
+    """The validator (llmdiy_qwdf_validate) accepts a well-formed file and names what is wrong with
+    bad ones: magic, length, a non-finite value (with its tensor), an unsupported config, a missing file."""
+    import json
+    import sys
+    d = tempfile.mkdtemp()
+    good = os.path.join(d, "good.bin")
+    L.write_random_bin(good, SMALL, seed=5)
+    r = L.validate_bin(good)
+    assert r["ok"] and r["status"] == 0 and r["nonfinite"] == 0, r
+    assert r["config"] == SMALL.as_dict()
+
+    data = bytearray(open(good, "rb").read())
+    magic = os.path.join(d, "magic.bin")
+    open(magic, "wb").write(b"XXXX" + bytes(data[4:]))
+    r = L.validate_bin(magic)
+    assert r["status"] == L.ERR_FORMAT and "magic" in r["message"], r
+
+    trunc = os.path.join(d, "trunc.bin")
+    open(trunc, "wb").write(bytes(data[:-2]))
+    r = L.validate_bin(trunc)
+    assert r["status"] == L.ERR_FORMAT and "truncated" in r["message"], r
+
+    # plant a NaN and an Inf in layer 0's qkv_w (tensor 2: after wte and ln_1)
+    H, V = SMALL.hidden_size, SMALL.vocab_size
+    off = 28 + 2 * (V * H + H) + 2 * 1000
+    nan = bytearray(data)
+    nan[off:off + 2] = (0x7E00).to_bytes(2, "little")
+    nan[off + 2:off + 4] = (0x7C00).to_bytes(2, "little")
+    pn = os.path.join(d, "nan.bin")
+    open(pn, "wb").write(bytes(nan))
+    r = L.validate_bin(pn)
+    assert r["status"] == L.ERR_FORMAT and r["nonfinite"] == 2 and "layer 0 qkv_w" in r["message"], r
+
+    trail = os.path.join(d, "trail.bin")
+    open(trail, "wb").write(bytes(data) + b"\0" * 6)
+    r = L.validate_bin(trail)
+    assert r["ok"] and "trailing" in r["message"], r
+
+    odd = L.make_config(vocab_size=64, hidden_size=256, num_layers=1, num_heads=2, intermediate_size=64,
+                        max_seqlen=8)
+    po = os.path.join(d, "odd.bin")
+    L.write_random_bin(po, odd, seed=1)
+    r = L.validate_bin(po)
+    assert r["status"] == L.ERR_UNSUPPORTED and "hidden_size 2048" in r["message"], r
+
+    r = L.validate_bin(os.path.join(d, "missing.bin"))
+    assert r["status"] == L.ERR_FILE and r["config"] is None, r
+
+    # the command-line form
+    cli = L.__file__
+    out = subprocess.run([sys.executable, cli, "validate", good], capture_output=True, text=True)
+    assert out.returncode == 0 and json.loads(out.stdout)["ok"], out
+    out = subprocess.run([sys.executable, cli, "validate", pn], capture_output=True, text=True)
+    assert out.returncode == 1 and not json.loads(out.stdout)["ok"], out
+    for f in (good, magic, trunc, pn, trail, po):
+        os.remove(f)
+
+
 def test_driver_reports_missing_weights():
     # qwen_infer.cu:121-124: an unreadable model file ends the process with status 1
     if not os.path.exists(L.DRIVER_PATH):
