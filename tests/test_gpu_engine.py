@@ -185,6 +185,36 @@ def test_driver_protocol(small_bin, engine):
     assert "invalid token id" in p.stderr
 
 
+def test_driver_batch_verb(small_bin, engine):
+    """The driver's "batch" verb (continuous batching, two slots for six requests): every request
+    gets its own turn's tokens, a malformed request is rejected, and plain turns still work after."""
+    env = dict(os.environ, LLMDIY_MAX_NEW_TOKENS="12", LLMDIY_IGNORE_EOS="1", LLMDIY_MAX_BATCH="2",
+               LLMDIY_BATCH_MAX_LEN="256")
+    prompts = [[5, 6, 7, 8], [9], [100, 200, 300], [11, 12], [1, 2, 3, 4, 5, 6, 7], [40, 41]]
+    lines = ["batch"] + [" ".join(map(str, q)) for q in prompts] + ["12 x", "end", "5 6 7 8", "exit"]
+    p = _run_driver(L.DRIVER_PATH, small_bin, lines, env=env)
+    assert p.returncode == 0, p.stderr
+    out = p.stdout.splitlines()
+    i0, i1 = out.index("[BATCH_START] 7"), out.index("[BATCH_END]")
+    got, done = {r: [] for r in range(7)}, []
+    for line in out[i0 + 1:i1]:
+        if line.startswith("[DONE] "):
+            done.append(int(line.split()[1]))
+        else:
+            r, t = map(int, line.split())
+            assert r not in done
+            got[r].append(t)
+    assert sorted(done) == list(range(7))
+    for r, q in enumerate(prompts):
+        want = engine.generate(q, 12, stop_on_eos=False)
+        assert len(got[r]) == 12, (r, got[r])
+        n_same = next((i for i, (a, b) in enumerate(zip(got[r], want)) if a != b), 12)
+        assert n_same >= 8, (r, got[r], want)  # batched GEMMs vs the GEMV decode: same greedy stream
+    assert got[6] == [] and "invalid token id" in p.stderr
+    turns = _parse_turns("\n".join(out[i1 + 1:]))
+    assert turns == [engine.generate([5, 6, 7, 8], 12, stop_on_eos=False)]
+
+
 def test_reference_engine_stream(small_bin, engine):
     """The reference engine, built from its sources as compute_89 PTX, on the same weights."""
     import oracle as orc
