@@ -139,15 +139,25 @@ __global__ void __launch_bounds__(256) splitk_reduce_k(const float* __restrict__
 }
 
 // ---------------------------------------------------------------- ragged split-KV attention
+// Work items are (sequence b, head h, split sp) over rows [sp*1024, min(len, (sp+1)*1024)).
+// Longest first: every full 1024-row split (16 tiles) is numbered before the partial last
+// splits, which follow in decreasing size.  CTAs claim items from a per-layer counter
+// (zeroed at the start of each step) as their producer thread needs them, so a CTA that
+// drew short items simply takes more: the grid finishes together.
+constexpr int kBQueue = 8;  // claimed items in flight per CTA (the producer runs <= kBStages tiles ahead)
+
 struct BFdSmem {
     half k[kBStages][kBRows * kHeadDim];
     half v[kBStages][kBRows * kHeadDim];
+    half qv[kBQueue][kHeadDim];  // query of each claimed item (bulk copy with its first tile)
     uint64_t full[kBStages];
     float so[4][kHeadDim];
     float sm[4], sl[4];
-    int pre[kBatchMax + 1];  // prefix sums of the items per sequence
-    int nsp[kBatchMax];      // splits per sequence
-    int len[kBatchMax];      // rows attended per sequence (pos + 1)
+    int qitem[kBQueue];       // claimed items in claim order (-1: no more)
+    int pre_full[kBatchMax + 1];  // prefix sums of full-split items per sequence
+    int order[kBatchMax];         // sequences with a partial last split, longest partial first
+    int len[kBatchMax];           // rows attended per sequence (pos + 1)
+    int nfull, nitems;
 };
 
 struct BItem {
@@ -156,57 +166,93 @@ struct BItem {
 };
 
 __device__ __forceinline__ void bfd_item(const BFdSmem& s, int item, int B, BItem& it) {
-    int b = 0;
-    while (b + 1 < B && s.pre[b + 1] <= item) ++b;
-    const int r = item - s.pre[b], S = s.nsp[b];
-    it.b = b;
-    it.h = r / S;
-    it.sp = r % S;
-    it.r0 = it.sp * kBSplitRows;
-    it.r1 = min(s.len[b], it.r0 + kBSplitRows);
+    if (item < s.nfull) {
+        int b = 0;
+        while (b + 1 < B && s.pre_full[b + 1] <= item) ++b;
+        const int r = item - s.pre_full[b];
+        it.b = b;
+        it.sp = r / kHeads;
+        it.h = r % kHeads;
+        it.r0 = it.sp * kBSplitRows;
+        it.r1 = it.r0 + kBSplitRows;
+    } else {
+        const int j = item - s.nfull, b = s.order[j / kHeads];
+        it.b = b;
+        it.h = j % kHeads;
+        it.sp = s.len[b] / kBSplitRows;
+        it.r0 = it.sp * kBSplitRows;
+        it.r1 = s.len[b];
+    }
     it.tile = 0;
     it.ntiles = (it.r1 - it.r0 + kBRows - 1) / kBRows;
 }
 
-// Items (sequence b, head h, split sp) over a persistent grid; each writes the
-// unnormalised partial (o[128], m, l) of its rows to part[((b*16 + h) * Smax + sp) * 130].
+// Each item writes the unnormalised partial (o[128], m, l) of its rows to
+// part[((b*16 + h) * Smax + sp) * 130]; bfd_merge_k combines a sequence's splits.
 __global__ void __launch_bounds__(128, 1)
     bfd_partials_k(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                    const half* __restrict__ q, const int* __restrict__ pos, int B, int max_len, int Smax,
-                   float* __restrict__ part, int* err) {
+                   float* __restrict__ part, int* ctr, int* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     BFdSmem& s = *reinterpret_cast<BFdSmem*>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hw = lane >> 4, dl = (lane & 15) * 8;
     const uint64_t pol = l2_policy_evict_first();
+    if (tid < B) s.len[tid] = pos[tid] + 1;
+    __syncthreads();
+    if (tid < B) {
+        // rank of this sequence's partial split among all partial splits (longer first, then lower b)
+        const int rb = s.len[tid] % kBSplitRows;
+        if (rb) {
+            int rank = 0;
+            for (int c = 0; c < B; ++c) {
+                const int rc = s.len[c] % kBSplitRows;
+                rank += rc > rb || (rc == rb && c < tid);
+            }
+            s.order[rank] = tid;
+        }
+    }
     if (tid == 0) {
         for (int i = 0; i < kBStages; ++i) mbar_init(&s.full[i], 1);
         mbar_fence_init();
-        int acc = 0;
+        int acc = 0, np = 0;
         for (int b = 0; b < B; ++b) {
-            s.len[b] = pos[b] + 1;
-            const int S = (s.len[b] + kBSplitRows - 1) / kBSplitRows;
-            s.nsp[b] = S;
-            s.pre[b] = acc;
-            acc += S * kHeads;
+            s.pre_full[b] = acc;
+            acc += (s.len[b] / kBSplitRows) * kHeads;
+            np += (s.len[b] % kBSplitRows) != 0;
         }
-        s.pre[B] = acc;
+        s.pre_full[B] = acc;
+        s.nfull = acc;
+        s.nitems = acc + np * kHeads;
     }
     __syncthreads();
-    const int nitems = s.pre[B], G = gridDim.x;
+    const int nitems = s.nitems;
+    // producer state (thread 0): the item being issued, claims made, tiles issued
     BItem pc;
-    uint32_t issued = 0, consumed = 0;
-    if (tid == 0 && (int)blockIdx.x < nitems) bfd_item(s, blockIdx.x, B, pc);
-    else pc.b = -1;
+    pc.tile = pc.ntiles = 0;
+    bool pdone = false;
+    uint32_t nclaimed = 0, issued = 0, consumed = 0;
     auto produce = [&]() {
-        if (pc.b < 0) return;
+        if (pdone) return;
+        bool first = false;
         while (pc.tile >= pc.ntiles) {
-            const int nxt = (int)(s.pre[pc.b] + pc.h * s.nsp[pc.b] + pc.sp) + G;  // this item's index + G
-            if (nxt >= nitems) { pc.b = -1; return; }
+            const int nxt = atomicAdd(ctr, 1);
+            if (nxt >= nitems) {
+                s.qitem[nclaimed % kBQueue] = -1;
+                ++nclaimed;
+                pdone = true;
+                return;
+            }
             bfd_item(s, nxt, B, pc);
+            s.qitem[nclaimed % kBQueue] = nxt;
+            ++nclaimed;
+            first = true;
         }
         const int st = issued % kBStages;
         const int y = pc.b * max_len + pc.r0 + pc.tile * kBRows;
-        mbar_arrive_expect_tx(&s.full[st], 2 * kBRows * kHeadDim * 2);
+        mbar_arrive_expect_tx(&s.full[st], 2 * kBRows * kHeadDim * 2 + (first ? kHeadDim * 2 : 0));
+        if (first)
+            bulk_g2s(s.qv[(nclaimed - 1) % kBQueue], q + (size_t)pc.b * kHidden + pc.h * kHeadDim, kHeadDim * 2,
+                     &s.full[st], pol);
         tma_load_2d_hint(s.k[st], &tk, pc.h * kHeadDim, y, &s.full[st], pol);
         tma_load_2d_hint(s.v[st], &tv, pc.h * kHeadDim, y, &s.full[st], pol);
         ++pc.tile;
@@ -214,14 +260,17 @@ __global__ void __launch_bounds__(128, 1)
     };
     if (tid == 0)
         for (int i = 0; i < kBStages; ++i) produce();
+    __syncthreads();  // the claims above are visible to every consumer
     const float scale = __frcp_rn(sqrtf((float)kHeadDim));
     bool failed = false;
-    for (int item = blockIdx.x; item < nitems && !failed; item += G) {
+    for (uint32_t qi = 0;; ++qi) {
+        // written by thread 0 at least one barrier ago (it claims an item when issuing its first
+        // tile, which is ahead of consumption; the end marker likewise)
+        const int item = s.qitem[qi % kBQueue];
+        if (item < 0) break;
         BItem it;
         bfd_item(s, item, B, it);
-        float q8[8];
-        unpack8(*reinterpret_cast<const uint4*>(q + (size_t)it.b * kHidden + it.h * kHeadDim + dl), q8);
-        float m = -INFINITY, l = 0.f, o8[8];
+        float q8[8], m = -INFINITY, l = 0.f, o8[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) o8[e] = 0.f;
         for (int t = 0; t < it.ntiles; ++t, ++consumed) {
@@ -231,6 +280,7 @@ __global__ void __launch_bounds__(128, 1)
                 failed = true;
                 break;
             }
+            if (t == 0) unpack8(*reinterpret_cast<const uint4*>(&s.qv[qi % kBQueue][dl]), q8);
             const int nvalid = min(kBRows, it.r1 - (it.r0 + t * kBRows));
             const half* kt = s.k[st];
             const half* vt = s.v[st];
@@ -273,7 +323,7 @@ __global__ void __launch_bounds__(128, 1)
                 }
                 m = mx;
             }
-            __syncthreads();
+            __syncthreads();  // every warp is done with stage st: refill it
             if (tid == 0) produce();
         }
         if (failed) break;
@@ -415,6 +465,7 @@ struct llmdiy_batch {
     size_t ws_floats = 0;
     float* fdp = nullptr;
     int *tok = nullptr, *pos = nullptr, *next = nullptr, *hist = nullptr, *step = nullptr, *err = nullptr;
+    int* ctr = nullptr;  // [num_layers] attention work counters
     int hist_steps = 0;
     half* pf = nullptr;  // prefill scratch (kPrefillChunk rows)
     std::vector<CUtensorMap> kmaps, vmaps;  // per layer, over [max_batch * max_len][H]
@@ -461,6 +512,9 @@ int gemm_rows(llmdiy_batch* b, const half* A, int lda, const half* W, int N, int
 int enqueue_step(llmdiy_batch* b, int B, cudaStream_t st) {
     const EngineView& v = b->v;
     const int NL = (int)v.cfg.num_layers, IM = (int)v.cfg.intermediate_size, V = (int)v.cfg.vocab_size;
+    // the attention's per-layer item counters start from zero every step
+    cudaError_t ce = cudaMemsetAsync(b->ctr, 0, sizeof(int) * NL, st);
+    if (ce != cudaSuccess) return (int)ce;
     embed_rows_k<<<B, 256, 0, st>>>(v.wte, b->tok, b->x);
     for (int l = 0; l < NL; ++l) {
         const LayerPtrs& L = v.layers[l];
@@ -471,7 +525,7 @@ int enqueue_step(llmdiy_batch* b, int B, cudaStream_t st) {
                            EpiQKVRows{L.qkv_b, b->q, kcl, vcl, b->pos, b->max_len}, st);
         if (rc) return rc;
         bfd_partials_k<<<v.num_sms, 128, sizeof(BFdSmem), st>>>(b->kmaps[l], b->vmaps[l], b->q, b->pos, B,
-                                                                 b->max_len, b->Smax, b->fdp, b->err);
+                                                                 b->max_len, b->Smax, b->fdp, b->ctr + l, b->err);
         bfd_merge_k<<<B * kHeads, kHeadDim, 0, st>>>(b->fdp, b->pos, b->Smax, b->att);
         rc = gemm_rows(b, b->att, kHidden, L.proj_w, kHidden, kHidden, B, EpiResidual{b->x}, st);
         if (rc) return rc;
@@ -538,6 +592,7 @@ int llmdiy_batch_create(llmdiy_engine* e, int max_batch, int max_len, llmdiy_bat
     alloc((void**)&b->next, kBatchMax * 4, "next");
     alloc((void**)&b->step, 4, "step");
     alloc((void**)&b->err, 4, "error word");
+    alloc((void**)&b->ctr, sizeof(int) * NL, "attention work counters");
     alloc((void**)&b->pf, (size_t)kPrefillChunk * (4 * H + IM) * 2, "prefill scratch");
     if (!rc) {
         b->kmaps.resize(NL);
@@ -583,7 +638,7 @@ void llmdiy_batch_destroy(llmdiy_batch* b) {
     if (b->graph) cudaGraphExecDestroy(b->graph);
     for (void* p : {(void*)b->kc, (void*)b->vc, (void*)b->x, (void*)b->xn, (void*)b->q, (void*)b->att, (void*)b->act,
                     (void*)b->logits, (void*)b->ws, (void*)b->fdp, (void*)b->tok, (void*)b->pos, (void*)b->next,
-                    (void*)b->hist, (void*)b->step, (void*)b->err, (void*)b->pf})
+                    (void*)b->hist, (void*)b->step, (void*)b->err, (void*)b->ctr, (void*)b->pf})
         if (p) cudaFree(p);
     delete b;
 }
