@@ -16,6 +16,7 @@
 
 #include "decode.h"
 #include "flash_prefill.cuh"
+#include "flash_tc.cuh"
 #include "gemm_tc_host.h"
 #include "ops.cuh"
 #include "prefill_tc.h"
@@ -76,8 +77,7 @@ int prefill_tc(const PrefillArgs& p, const int* tokens_dev, int n, int p0, cudaS
     cudaError_t e;
     static std::once_flag attr;
     std::call_once(attr, [] {
-        cudaFuncSetAttribute(flash_prefill_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sizeof(FlashPrefillSmem));
+        cudaFuncSetAttribute(flash_tc_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(FlashTcSmem));
     });
     for (int c0 = 0; c0 < n; c0 += kPrefillChunk) {
         const int m = n - c0 < kPrefillChunk ? n - c0 : kPrefillChunk;
@@ -91,8 +91,13 @@ int prefill_tc(const PrefillArgs& p, const int* tokens_dev, int n, int p0, cudaS
             rc = launch_gemm_tc(p.xn, kHidden, L.qkv_w, kHidden, m, 3 * kHidden, kHidden,
                                 EpiQKV{L.qkv_b, p.q, kcl, vcl, pos0}, st);
             if (rc) return rc;
-            flash_prefill_k<<<dim3((m + kFpRows - 1) / kFpRows, kHeads), kFpThreads, sizeof(FlashPrefillSmem), st>>>(
-                p.q, kcl, vcl, p.att, m, pos0, kHidden, kHidden);
+            CUtensorMap tq, tk, tv;
+            if (!make_kmajor_map(&tq, p.q, m, kHidden, kHidden, kFtRows) ||
+                !make_kmajor_map(&tk, kcl, p.max_seqlen, kHidden, kHidden, kFtKeys) ||
+                !make_kmajor_map(&tv, vcl, p.max_seqlen, kHidden, kHidden, kFtKeys))
+                return (int)cudaErrorInvalidValue;
+            flash_tc_k<<<dim3((m + kFtRows - 1) / kFtRows, kHeads), kFtThreads, sizeof(FlashTcSmem), st>>>(
+                tq, tk, tv, p.att, m, pos0, gemm_err_word());
             rc = launch_gemm_tc(p.att, kHidden, L.proj_w, kHidden, m, kHidden, kHidden, EpiResidual{p.x}, st);
             if (rc) return rc;
             rmsnorm_rows_k<<<m, 256, 0, st>>>(p.xn, p.x, L.ln2);
