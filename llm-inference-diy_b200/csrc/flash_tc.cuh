@@ -4,13 +4,13 @@
 // positions p0 .. p0+n-1 attending cache rows [0, pos] in place (no gather pass).
 //
 // CTA = 128 query rows of one head.  Warp 4 (one lane) loads Q once and streams
-// 64-key K/V tiles through a 2-stage TMA ring, and issues the MMAs:
+// 64-key K and V tiles through 2-stage TMA rings, and issues the MMAs:
 //   S(j)  = Q K(j)^T          128 x 64,  K = 128 dims  -> TMEM (two S buffers)
-//   O    += P(j-1) V(j-1)     128 x 128, K = 64 keys   -> TMEM (one O accumulator)
+//   O    += P(j) V(j)         128 x 128, K = 64 keys   -> TMEM (one O accumulator; P from TMEM)
 // with S(j+1) issued before PV(j), so the rows find it ready when they finish softmax(j).  Warps 0-3 own the query rows
 // (thread = row = TMEM lane): each reads its S row, applies the causal mask and the
-// online softmax in base 2, writes its P row (fp16) into shared memory in the MMA's
-// swizzled K-major layout, and signals the issuer.  O is rescaled (TMEM load, scale,
+// online softmax in base 2, writes its P row (fp16 pairs) back into TMEM over its S row,
+// where PV takes it as the A operand, and signals the issuer.  O is rescaled (TMEM load, scale,
 // store) only when a row's running maximum grows by more than 2^8; otherwise the stale
 // maximum is kept, which leaves O / l unchanged (P stays <= 256, exact in fp16 range).
 // At the end each thread reads its O row, divides by l and stores fp16.
@@ -30,6 +30,11 @@ constexpr int kFtKeys = 64;      // keys per tile
 constexpr int kFtStages = 2;     // K/V tiles in flight (two CTAs share an SM: 112 KB of smem each)
 constexpr int kFtThreads = 160;  // warps 0-3: rows (TMEM lanes 32w..32w+31); warp 4: TMA + MMA issue
 
+LLMDIY_DEV uint32_t pack_h2f(float lo, float hi) {  // two fp16 (round to nearest) in one 32-bit word
+    const half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 LLMDIY_DEV float ex2_approx(float x) {  // 2^x (the MUFU approximation; 2^-inf = 0)
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -40,8 +45,8 @@ struct FlashTcSmem {
     half q[2][kFtRows * 64];             // dims 0-63 | 64-127: K-major, 128-byte swizzle (16 KB each)
     half k[kFtStages][2][kFtKeys * 64];  // per stage, dims 0-63 | 64-127, K-major (8 KB each)
     half v[kFtStages][2][kFtKeys * 64];  // per stage, dims 0-63 | 64-127, MN-major (8 KB each)
-    half p[kFtRows * kFtKeys];           // P tile (128 rows x 64 keys), K-major, swizzled (16 KB)
-    uint64_t q_full, kv_full[kFtStages], kv_empty[kFtStages], s_full[2], p_full[2], o_done[2], drain;
+    uint64_t q_full, k_full[kFtStages], k_empty[kFtStages], v_full[kFtStages], v_empty[kFtStages];
+    uint64_t s_full[2], p_full[2], o_done[2], drain;
     uint32_t tmem_base;
     int fail;
 };
@@ -62,8 +67,10 @@ __global__ void __launch_bounds__(kFtThreads, 2)
     if (tid == 0) {
         mbar_init(&s.q_full, 1);
         for (int i = 0; i < kFtStages; ++i) {
-            mbar_init(&s.kv_full[i], 1);
-            mbar_init(&s.kv_empty[i], 1);
+            mbar_init(&s.k_full[i], 1);
+            mbar_init(&s.k_empty[i], 1);
+            mbar_init(&s.v_full[i], 1);
+            mbar_init(&s.v_empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s.s_full[i], 1);
@@ -87,40 +94,50 @@ __global__ void __launch_bounds__(kFtThreads, 2)
     if (warp == 4) {
         if (lane == 0) {
             // ---------------- producer + MMA issuer
-            int loaded = 0;  // K/V tiles whose loads were issued
-            auto load_kv = [&](int j) {
-                const int st = j % kFtStages, y = j * kFtKeys;
-                mbar_arrive_expect_tx(&s.kv_full[st], 4 * kFtKeys * 64 * 2);
-                tma_load_2d(s.k[st][0], &tk, h * kHeadDim, y, &s.kv_full[st]);
-                tma_load_2d(s.k[st][1], &tk, h * kHeadDim + 64, y, &s.kv_full[st]);
-                tma_load_2d(s.v[st][0], &tv, h * kHeadDim, y, &s.kv_full[st]);
-                tma_load_2d(s.v[st][1], &tv, h * kHeadDim + 64, y, &s.kv_full[st]);
-                ++loaded;
+            // K and V tiles have their own rings: K(t) can stream in as soon as S(t-2) is done,
+            // well before PV(t-2) releases V's stage
+            int kloaded = 0, vloaded = 0;
+            auto load_k = [&](int t) {
+                const int st = t % kFtStages, y = t * kFtKeys;
+                mbar_arrive_expect_tx(&s.k_full[st], 2 * kFtKeys * 64 * 2);
+                tma_load_2d(s.k[st][0], &tk, h * kHeadDim, y, &s.k_full[st]);
+                tma_load_2d(s.k[st][1], &tk, h * kHeadDim + 64, y, &s.k_full[st]);
+                ++kloaded;
+            };
+            auto load_v = [&](int t) {
+                const int st = t % kFtStages, y = t * kFtKeys;
+                mbar_arrive_expect_tx(&s.v_full[st], 2 * kFtKeys * 64 * 2);
+                tma_load_2d(s.v[st][0], &tv, h * kHeadDim, y, &s.v_full[st]);
+                tma_load_2d(s.v[st][1], &tv, h * kHeadDim + 64, y, &s.v_full[st]);
+                ++vloaded;
             };
             mbar_arrive_expect_tx(&s.q_full, 2 * kFtRows * 64 * 2);
             tma_load_2d(s.q[0], &tq, h * kHeadDim, q0, &s.q_full);
             tma_load_2d(s.q[1], &tq, h * kHeadDim + 64, q0, &s.q_full);
-            for (int j = 0; j < T && j < kFtStages; ++j) load_kv(j);
+            for (int t = 0; t < T && t < kFtStages; ++t) load_k(t);
+            for (int t = 0; t < T && t < kFtStages; ++t) load_v(t);
             constexpr uint32_t idS = umma_idesc_f16_f32(kFtRows, kFtKeys, false);
             constexpr uint32_t idO = umma_idesc_f16_f32(kFtRows, kHeadDim, true);
             const uint32_t qa = smem_u32(s.q[0]);
             bool ok = mbar_wait(&s.q_full, 0, &s.fail);
-            auto pv = [&](int i) -> bool {  // O += P(i) V(i), then release P(i)'s buffer and K/V(i)'s stage
+            auto pv = [&](int i) -> bool {  // O += P(i) V(i), then release the P tile and V(i)'s stage
                 if (!mbar_wait(&s.p_full[i & 1], (i >> 1) & 1, &s.fail)) return false;
+                if (!mbar_wait(&s.v_full[i % kFtStages], (i / kFtStages) & 1, &s.fail)) return false;
                 tc_fence_after();
-                const uint32_t pa = smem_u32(s.p), vb = smem_u32(s.v[i % kFtStages][0]);
+                // A = P(i) in TMEM (packed over S(i)'s first 32 columns), B = V(i) in shared memory
+                const uint32_t pa = tmem + 64u * (i & 1), vb = smem_u32(s.v[i % kFtStages][0]);
 #pragma unroll
                 for (int kk = 0; kk < kFtKeys / 16; ++kk)
-                    umma_f16(tO, umma_desc_sw128(pa + 32 * kk), umma_desc_sw128_mn(vb + 2048 * kk, 8192, 1024), idO,
-                             (i | kk) != 0 ? 1u : 0u);
+                    umma_f16_tmem_a(tO, pa + 8 * kk, umma_desc_sw128_mn(vb + 2048 * kk, 8192, 1024), idO,
+                                    (i | kk) != 0 ? 1u : 0u);
                 umma_commit(&s.o_done[i & 1]);
-                umma_commit(&s.kv_empty[i % kFtStages]);
+                umma_commit(&s.v_empty[i % kFtStages]);
                 return true;
             };
-            // S(j) = Q K(j)^T into TMEM buffer j & 1
+            // S(j) = Q K(j)^T into TMEM buffer j & 1, then release K(j)'s stage
             auto qk = [&](int j) -> bool {
                 const int st = j % kFtStages;
-                if (!mbar_wait(&s.kv_full[st], (j / kFtStages) & 1, &s.fail)) return false;
+                if (!mbar_wait(&s.k_full[st], (j / kFtStages) & 1, &s.fail)) return false;
                 tc_fence_after();
                 const uint32_t kb = smem_u32(s.k[st][0]);
 #pragma unroll
@@ -128,19 +145,28 @@ __global__ void __launch_bounds__(kFtThreads, 2)
                     umma_f16(tmem + 64u * (j & 1), umma_desc_sw128(qa + (kk >> 2) * 16384 + 32 * (kk & 3)),
                              umma_desc_sw128(kb + (kk >> 2) * 8192 + 32 * (kk & 3)), idS, kk != 0 ? 1u : 0u);
                 umma_commit(&s.s_full[j & 1]);
+                umma_commit(&s.k_empty[st]);
                 return true;
             };
             if (ok && !qk(0)) ok = false;
             for (int j = 0; ok && j < T; ++j) {
-                // refill the stage PV(j-1) released with tile j-1+kFtStages
-                const int i = j - 1;
-                if (i >= 0 && i + kFtStages < T) {
-                    if (!mbar_wait(&s.kv_empty[i % kFtStages], (i / kFtStages) & 1, &s.fail)) { ok = false; break; }
-                    load_kv(i + kFtStages);
+                // K(j+2) into the stage S(j) released (S(j) was issued an iteration ago)
+                if (j + kFtStages < T) {
+                    if (!mbar_wait(&s.k_empty[j % kFtStages], (j / kFtStages) & 1, &s.fail)) { ok = false; break; }
+                    load_k(j + kFtStages);
                 }
                 // S(j+1) before PV(j), so it is ready when the rows finish softmax(j); its TMEM
-                // buffer was last read by softmax(j-1), which completed before PV(j-1) was issued
-                if (j + 1 < T && !qk(j + 1)) { ok = false; break; }
+                // buffer held P(j-1): PV(j-1) must be complete
+                if (j + 1 < T) {
+                    const bool freed = j < 1 || mbar_wait(&s.o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, &s.fail);
+                    if (!freed || !qk(j + 1)) { ok = false; break; }
+                }
+                // V(j+1) into the stage PV(j-1) released
+                const int i = j - 1;
+                if (i >= 0 && i + kFtStages < T) {
+                    if (!mbar_wait(&s.v_empty[i % kFtStages], (i / kFtStages) & 1, &s.fail)) { ok = false; break; }
+                    load_v(i + kFtStages);
+                }
                 if (!pv(j)) { ok = false; break; }
             }
             if (!ok) {
@@ -148,8 +174,10 @@ __global__ void __launch_bounds__(kFtThreads, 2)
                 // every MMA issued so far, and the copies that no MMA consumed, complete before the CTA exits
                 umma_commit(&s.drain);
                 (void)mbar_wait(&s.drain, 0);
-                for (int j = loaded > kFtStages ? loaded - kFtStages : 0; j < loaded; ++j)
-                    (void)mbar_wait(&s.kv_full[j % kFtStages], (j / kFtStages) & 1);
+                for (int t = kloaded > kFtStages ? kloaded - kFtStages : 0; t < kloaded; ++t)
+                    (void)mbar_wait(&s.k_full[t % kFtStages], (t / kFtStages) & 1);
+                for (int t = vloaded > kFtStages ? vloaded - kFtStages : 0; t < vloaded; ++t)
+                    (void)mbar_wait(&s.v_full[t % kFtStages], (t / kFtStages) & 1);
                 (void)mbar_wait(&s.q_full, 0);
             }
         }
@@ -203,25 +231,24 @@ __global__ void __launch_bounds__(kFtThreads, 2)
                 l *= f;
                 m = mt;
             }
-            // P(j) overwrites P(j-1): PV(j-1) must have read it
-            if (j >= 1 && !mbar_wait(&s.o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, &s.fail)) { ok = false; break; }
-            uint8_t* prow = reinterpret_cast<uint8_t*>(s.p) + r * 128;
+            // P(j) in fp16 pairs over the first 32 columns of S(j)'s buffer (S(j) is in registers)
             const float nm = -m;
             float ls[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) ls[e] = 0.f;
+            uint32_t pk[kFtKeys / 2];
 #pragma unroll
-            for (int c8 = 0; c8 < kFtKeys / 8; ++c8) {
-                float pv8[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    pv8[e] = ex2_approx(__fmaf_rn(x[8 * c8 + e], kScaleLog2, nm));  // masked keys: 2^-inf = 0
-                    ls[e] += pv8[e];
-                }
-                *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = pack8(pv8);
+            for (int c = 0; c < kFtKeys; c += 2) {
+                const float p0 = ex2_approx(__fmaf_rn(x[c], kScaleLog2, nm));  // masked keys: 2^-inf = 0
+                const float p1 = ex2_approx(__fmaf_rn(x[c + 1], kScaleLog2, nm));
+                ls[c & 7] += p0;
+                ls[(c + 1) & 7] += p1;
+                pk[c / 2] = pack_h2f(p0, p1);
             }
             l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
-            fence_proxy_async_smem();
+#pragma unroll
+            for (int c = 0; c < kFtKeys / 2; c += 16) tmem_st16(tmem + 64u * (j & 1) + lane_off + c, pk + c);
+            tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&s.p_full[j & 1]);
         }
