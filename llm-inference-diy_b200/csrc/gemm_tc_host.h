@@ -8,6 +8,7 @@
 #include <mutex>
 
 #include "gemm_tc.cuh"
+#include "gemm_tc2.cuh"
 
 namespace llmdiy {
 constexpr int kGemmBN = 256;  // output columns per CTA tile (UMMA N = 256)
@@ -20,10 +21,30 @@ int gemm_tc_status();  // 0, or 1 once any GEMM of this device recorded an expir
 
 // C tile op `epi` is called per thread with (row, first column, 16 fp32 values).
 // ksplit > 1: grid.z slices of the K blocks, each running `epi` on its partial sums.
+// M > 128 without split-K: 2-CTA clusters, 256 x 256 tiles per pair (gemm_tc2.cuh).
+template <class Epi>
+int launch_gemm_tc2(const half* A, int lda, const half* W, int ldw, int M, int N, int K, const Epi& epi,
+                    cudaStream_t st) {
+    CUtensorMap ta, tb;
+    if (!make_kmajor_map(&ta, A, M, K, lda, 128) || !make_kmajor_map(&tb, W, N, K, ldw, 128))
+        return (int)cudaErrorInvalidValue;
+    int* err = gemm_err_word();
+    if (!err) return (int)cudaErrorMemoryAllocation;
+    auto kern = gemm_tc2_k<Epi>;
+    static std::once_flag attr;
+    std::call_once(attr, [&] {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Gemm2Smem));
+    });
+    dim3 grid(2 * ((N + 255) / 256), (M + 255) / 256, 1);
+    kern<<<grid, kGemmThreads, sizeof(Gemm2Smem), st>>>(ta, tb, M, N, K, epi, err);
+    return (int)cudaGetLastError();
+}
+
 template <class Epi>
 int launch_gemm_tc(const half* A, int lda, const half* W, int ldw, int M, int N, int K, const Epi& epi,
                    cudaStream_t st, int ksplit = 1) {
     if (M <= 0 || N <= 0 || K <= 0) return (int)cudaErrorInvalidValue;
+    if (ksplit == 1 && M > kGemmBM) return launch_gemm_tc2(A, lda, W, ldw, M, N, K, epi, st);
     constexpr int BN = kGemmBN;
     CUtensorMap ta, tb;
     if (!make_kmajor_map(&ta, A, M, K, lda, kGemmBM) || !make_kmajor_map(&tb, W, N, K, ldw, BN))
