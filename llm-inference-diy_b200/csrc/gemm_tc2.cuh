@@ -7,9 +7,10 @@
 //
 // Roles, per CTA: warp 0 lane 0 loads its halves (TMA, completing on the LEADER's full
 // barrier, which expects both CTAs' bytes); in the leader (rank 0) warp 1 lane 0 issues the
-// MMAs and commits to both CTAs' empty / accumulator barriers; warps 0-3 run the epilogue on
-// their TMEM lanes.  Every wait is bounded; a CTA whose wait expires records an error, and
-// both CTAs still meet at the final cluster barrier.
+// MMAs and commits to both CTAs' empty / accumulator barriers; warps 2-5 run the epilogue on
+// their TMEM lanes and release the accumulator buffer on the leader's barrier.  Every wait is
+// bounded; a CTA whose wait expires records an error, and both CTAs still meet at the final
+// cluster barrier.
 #pragma once
 #include <cuda.h>
 
@@ -24,7 +25,8 @@ struct Gemm2Smem {
     half b[kGemm2Stages][128 * kGemmBK];  // 16 KB per stage (this CTA's half of the B tile)
     uint64_t full[kGemm2Stages];          // used in the leader: both CTAs' loads complete here
     uint64_t empty[kGemm2Stages];         // each CTA: the pair's MMAs are done with the stage
-    uint64_t accum;                       // each CTA: the accumulator is final
+    uint64_t acc_full[2];                 // each CTA: accumulator buffer b holds a finished tile
+    uint64_t acc_empty[2];                // leader: both CTAs' epilogues have drained buffer b
     uint32_t tmem_base;
     int fail;
 };
@@ -69,8 +71,13 @@ LLMDIY_DEV void umma2_commit_both(uint64_t* bar) {
         : "memory");
 }
 
+constexpr int kGemm2Threads = 192;  // warp 0: TMA, warp 1: MMA (leader), warps 2-5: epilogue
+
+// Persistent: pair p of the grid's pairs takes pair tiles t = p, p + pairs, ... (256 x 256 output
+// each; t runs down the M tiles of one N column first).  The accumulator is double-buffered in
+// TMEM (2 x 256 columns), so the epilogue of tile i overlaps the MMAs of tile i+1.
 template <class Epi>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
     gemm_tc2_k(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmb, int M, int N, int K,
                Epi epi, int* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -78,18 +85,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
-    const int pair_n = (int)blockIdx.x >> 1;
-    const int m0 = (int)blockIdx.y * 256 + (int)rank * 128;  // this CTA's A rows = its output rows
-    const int nb = pair_n * 256 + (int)rank * 128;           // this CTA's half of the B tile
-    const int nout = pair_n * 256;                           // the pair's output columns
+    const int pair = (int)blockIdx.x >> 1, pairs = (int)gridDim.x >> 1;
+    const int nTM = (M + 255) / 256, nTN = (N + 255) / 256, T = nTM * nTN;
     const int KB = (K + kGemmBK - 1) / kGemmBK;
-    constexpr uint32_t kCols = 256;
+    constexpr uint32_t kCols = 512;
     if (tid == 0) {
         for (int i = 0; i < kGemm2Stages; ++i) {
             mbar_init(&s.full[i], 1);
             mbar_init(&s.empty[i], 1);
         }
-        mbar_init(&s.accum, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s.acc_full[i], 1);
+            mbar_init(&s.acc_empty[i], 2 * 128);  // both CTAs' epilogue threads (used in the leader)
+        }
         s.fail = 0;
         mbar_fence_init();
     }
@@ -104,68 +112,89 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
 
-    int issued = 0;
-    if (warp == 0 && lane == 0) {
-        // ---------------- producer (both CTAs)
-        for (int kb = 0; kb < KB; ++kb) {
-            const int st = kb % kGemm2Stages;
-            if (kb >= kGemm2Stages && !mbar_wait(&s.empty[st], ((kb / kGemm2Stages) - 1) & 1, &s.fail)) {
-                s.fail = 1;
-                break;
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- producer (both CTAs): this CTA's halves of every k-block of every tile
+            int g = 0;
+            for (int t = pair; t < T && !s.fail; t += pairs) {
+                const int m0 = (t % nTM) * 256 + (int)rank * 128, nb = (t / nTM) * 256 + (int)rank * 128;
+                for (int kb = 0; kb < KB; ++kb, ++g) {
+                    const int st = g % kGemm2Stages;
+                    if (g >= kGemm2Stages && !mbar_wait(&s.empty[st], ((g / kGemm2Stages) - 1) & 1, &s.fail)) {
+                        s.fail = 1;
+                        break;
+                    }
+                    // the leader's full barrier expects both CTAs' bytes; its own arrive carries the count
+                    if (leader) mbar_arrive_expect_tx(&s.full[st], 2 * 2 * 128 * kGemmBK * 2);
+                    const uint32_t bar = map_to_rank(&s.full[st], 0);
+                    tma_load_2d_pair(s.a[st], &tma, kb * kGemmBK, m0, bar);
+                    tma_load_2d_pair(s.b[st], &tmb, kb * kGemmBK, nb, bar);
+                }
             }
-            // the leader's full barrier expects both CTAs' bytes; its own arrive carries the count
-            if (leader) mbar_arrive_expect_tx(&s.full[st], 2 * 2 * 128 * kGemmBK * 2);
-            const uint32_t bar = map_to_rank(&s.full[st], 0);
-            tma_load_2d_pair(s.a[st], &tma, kb * kGemmBK, m0, bar);
-            tma_load_2d_pair(s.b[st], &tmb, kb * kGemmBK, nb, bar);
-            ++issued;
         }
-    } else if (warp == 1 && lane == 0 && leader) {
-        // ---------------- MMA issuer (leader only): 256 x 256 x 16 per instruction
-        constexpr uint32_t idesc = umma_idesc_f16_f32(256, 256, false);
-        int kb = 0;
-        for (; kb < KB; ++kb) {
-            const int st = kb % kGemm2Stages;
-            if (!mbar_wait(&s.full[st], (kb / kGemm2Stages) & 1, &s.fail)) {
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ---------------- MMA issuer (leader only): 256 x 256 x 16 per instruction
+            constexpr uint32_t idesc = umma_idesc_f16_f32(256, 256, false);
+            int g = 0, it = 0;
+            bool ok = true;
+            for (int t = pair; ok && t < T; t += pairs, ++it) {
+                const int buf = it & 1;
+                // both CTAs' epilogues are done with this accumulator (used two tiles ago)
+                if (it >= 2 && !mbar_wait(&s.acc_empty[buf], ((it >> 1) - 1) & 1, &s.fail)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t acc = tmem + 256u * buf;
+                for (int kb = 0; kb < KB; ++kb, ++g) {
+                    const int st = g % kGemm2Stages;
+                    if (!mbar_wait(&s.full[st], (g / kGemm2Stages) & 1, &s.fail)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(s.a[st]), b0 = smem_u32(s.b[st]);
+#pragma unroll
+                    for (int k = 0; k < kGemmBK / 16; ++k)
+                        umma2_f16(acc, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc,
+                                  (kb | k) != 0);
+                    umma2_commit_both(&s.empty[st]);  // both CTAs may refill the stage once these MMAs read it
+                }
+                umma2_commit_both(&s.acc_full[buf]);  // the tile's accumulator, in both CTAs
+            }
+            if (!ok) s.fail = 1;
+        }
+    } else {
+        // ---------------- epilogue (warps 2-5 of both CTAs): TMEM lanes 32q .. 32q+31
+        const int q = warp & 3;
+        const uint32_t empty_leader = map_to_rank(&s.acc_empty[0], 0);
+        int it = 0;
+        for (int t = pair; t < T; t += pairs, ++it) {
+            const int buf = it & 1;
+            if (!mbar_wait(&s.acc_full[buf], (it >> 1) & 1, &s.fail)) {
                 s.fail = 1;
                 break;
             }
             tc_fence_after();
-            const uint32_t a0 = smem_u32(s.a[st]), b0 = smem_u32(s.b[st]);
-#pragma unroll
-            for (int k = 0; k < kGemmBK / 16; ++k)
-                umma2_f16(tmem, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc, (kb | k) != 0);
-            umma2_commit_both(&s.empty[st]);  // both CTAs may refill the stage once these MMAs read it
+            const int row = (t % nTM) * 256 + (int)rank * 128 + q * 32 + lane, n0 = (t / nTM) * 256;
+            const uint32_t lane_addr = tmem + 256u * buf + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < 256; c += 16) {
+                if (n0 + c >= N) break;  // warp-uniform
+                uint32_t r[16];
+                tmem_ld16(lane_addr + (uint32_t)c, r);
+                tmem_ld_wait();
+                if (row < M) epi(row, n0 + c, reinterpret_cast<const float*>(r));
+            }
+            tc_fence_before();
+            // release the buffer in the leader (cluster-scope arrive on its barrier)
+            asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+                         ::"r"(empty_leader + 8u * buf)
+                         : "memory");
         }
-        umma2_commit_both(&s.accum);  // all MMAs issued so far (a failed loop commits what it has)
     }
     __syncwarp();
-    // ---------------- epilogue (both CTAs): rows m0 .. m0+127, the pair's 256 columns
-    const bool ok = __syncthreads_and(mbar_wait(&s.accum, 0, &s.fail) && !s.fail);
-    tc_fence_after();
-    if (ok) {
-        const int row = m0 + warp * 32 + lane;
-        const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-#pragma unroll 1
-        for (int c = 0; c < 256; c += 16) {
-            if (nout + c >= N) break;  // warp-uniform
-            uint32_t r[16];
-            tmem_ld16(lane_addr + (uint32_t)c, r);
-            tmem_ld_wait();
-            if (row < M) epi(row, nout + c, reinterpret_cast<const float*>(r));
-        }
-    } else if (tid == 0) {
-        atomicExch(err, 1);
-    }
-    // after a failure, loads that no MMA consumed must land before either CTA exits: they all
-    // complete on the leader's full barriers (bounded waits; the final cluster barrier holds the peer)
-    if (warp == 0 && lane == 0 && !ok && leader) {
-        for (int kb = issued > kGemm2Stages ? issued - kGemm2Stages : 0; kb < issued; ++kb)
-            (void)mbar_wait(&s.full[kb % kGemm2Stages], (kb / kGemm2Stages) & 1);
-    }
     tc_fence_before();
     __syncthreads();
-    cluster_sync_all();  // the peer's MMAs and loads no longer touch this CTA's shared memory
+    if (tid == 0 && s.fail) atomicExch(err, 1);
+    // the peer's MMAs and loads no longer touch this CTA's shared memory or TMEM after this point
+    // (every MMA was waited for through acc_full; a failed run waits out its bounded waits first)
+    cluster_sync_all();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
 }

@@ -5,6 +5,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "gemm_tc.cuh"
@@ -21,7 +22,17 @@ int gemm_tc_status();  // 0, or 1 once any GEMM of this device recorded an expir
 
 // C tile op `epi` is called per thread with (row, first column, 16 fp32 values).
 // ksplit > 1: grid.z slices of the K blocks, each running `epi` on its partial sums.
-// M > 128 without split-K: 2-CTA clusters, 256 x 256 tiles per pair (gemm_tc2.cuh).
+inline int gemm_num_sms() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    return sms;
+}
+
+// M > 128 without split-K: persistent 2-CTA clusters, 256 x 256 tiles per pair (gemm_tc2.cuh).
 template <class Epi>
 int launch_gemm_tc2(const half* A, int lda, const half* W, int ldw, int M, int N, int K, const Epi& epi,
                     cudaStream_t st) {
@@ -35,8 +46,10 @@ int launch_gemm_tc2(const half* A, int lda, const half* W, int ldw, int M, int N
     std::call_once(attr, [&] {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Gemm2Smem));
     });
-    dim3 grid(2 * ((N + 255) / 256), (M + 255) / 256, 1);
-    kern<<<grid, kGemmThreads, sizeof(Gemm2Smem), st>>>(ta, tb, M, N, K, epi, err);
+    const int sms = gemm_num_sms();
+    const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    const int pairs = std::max(1, std::min(tiles, sms / 2));
+    kern<<<2 * pairs, kGemm2Threads, sizeof(Gemm2Smem), st>>>(ta, tb, M, N, K, epi, err);
     return (int)cudaGetLastError();
 }
 
@@ -44,7 +57,10 @@ template <class Epi>
 int launch_gemm_tc(const half* A, int lda, const half* W, int ldw, int M, int N, int K, const Epi& epi,
                    cudaStream_t st, int ksplit = 1) {
     if (M <= 0 || N <= 0 || K <= 0) return (int)cudaErrorInvalidValue;
-    if (ksplit == 1 && M > kGemmBM) return launch_gemm_tc2(A, lda, W, ldw, M, N, K, epi, st);
+    // SM pairs when there are at least as many 256 x 256 tiles as pairs (below that, 128 x 256
+    // tiles on single SMs cover more of the GPU)
+    if (ksplit == 1 && M > kGemmBM && ((M + 255) / 256) * ((N + 255) / 256) >= gemm_num_sms() / 2)
+        return launch_gemm_tc2(A, lda, W, ldw, M, N, K, epi, st);
     constexpr int BN = kGemmBN;
     CUtensorMap ta, tb;
     if (!make_kmajor_map(&ta, A, M, K, lda, kGemmBM) || !make_kmajor_map(&tb, W, N, K, ldw, BN))
