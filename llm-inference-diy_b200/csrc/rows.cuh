@@ -20,11 +20,12 @@ static __global__ void __launch_bounds__(256) rmsnorm_rows_k(half* __restrict__ 
                                                       const half* __restrict__ w) {
     __shared__ float red[17];
     const int r = blockIdx.x, t = threadIdx.x;
-    const half* xr = x + (size_t)r * kHidden;
-    const float s = rms_scale_tree256(xr, kHidden, 1e-6f, red, t, 1);
+    const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)r * kHidden + 8 * t);  // this thread's 8 values
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * t);
+    const float s = rms_scale_regs2048(v, 1e-6f, red, t, 1);
     float xf[8], wf[8], of[8];
-    unpack8(*reinterpret_cast<const uint4*>(xr + 8 * t), xf);
-    unpack8(*reinterpret_cast<const uint4*>(w + 8 * t), wf);
+    unpack8(v, xf);
+    unpack8(wv, wf);
 #pragma unroll
     for (int e = 0; e < 8; ++e) of[e] = (xf[e] * s) * wf[e];
     *reinterpret_cast<uint4*>(out + (size_t)r * kHidden + 8 * t) = pack8(of);
