@@ -85,6 +85,24 @@ int llmdiy_fd_mh_merge(const float* parts, int G, int num_heads, uint16_t* O, vo
  * workspace expired (its output is then not valid). */
 int llmdiy_fd_mh_status(const float* work, int L, int num_heads);
 
+/* Multi-GPU exchange of the shards' partials over peer memory (no counterpart in the reference,
+ * which has no multi-GPU path; replaces an all-gather + llmdiy_fd_mh_merge).  Every rank owns a
+ * receive buffer of llmdiy_p2p_buffer_bytes(world, num_heads) bytes ([world][num_heads][130] fp32
+ * partials, then [world][num_heads] u32 flags), allocated with llmdiy_p2p_alloc, whose CUDA IPC
+ * handle (64 bytes) the other ranks open with llmdiy_p2p_open.  llmdiy_fd_p2p_merge, called by every
+ * rank with the same tag (a call counter starting at 1), stores this rank's [num_heads][130] partial
+ * into slot `rank` of every rank's buffer (peers[] = device array of the world buffer pointers in rank
+ * order, this rank's own included), raises its flags there, waits (bounded) for every rank's flags in
+ * its own buffer, and merges the partials in rank order into O.  *err (device int) becomes 1 when a
+ * wait expired.  The ranks' kernels must run on different GPUs. */
+size_t llmdiy_p2p_buffer_bytes(int world, int num_heads);
+int llmdiy_p2p_alloc(size_t bytes, void** ptr, uint8_t* ipc_handle /* 64 bytes out */);
+int llmdiy_p2p_open(const uint8_t* ipc_handle /* 64 bytes */, void** ptr);
+int llmdiy_p2p_close(void* peer_ptr);
+int llmdiy_p2p_free(void* ptr);
+int llmdiy_fd_p2p_merge(const float* part, const uint64_t* peers, int world, int rank, int num_heads, uint32_t tag,
+                        uint16_t* O, int* err, void* stream);
+
 /* No counterpart in the reference.  Split-KV flash decoding of one head in a single launch that
  * allocates nothing: the same result, bit for bit, as llmdiy_fd_v5_split_stage1 + llmdiy_fd_opt_stage2
  * with num_chunks = ceil(L/256), but the chunk partials live in a file-scope device array (33,536 bytes)

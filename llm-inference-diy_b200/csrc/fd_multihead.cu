@@ -12,6 +12,7 @@
 // exchanges (NCCL all-gather) before the final merge of the shards' partials.
 #include <cuda.h>
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "llmdiy_kernels.h"
@@ -294,6 +295,52 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_merge_ranks_k(const float* __re
                   nullptr);
 }
 
+// Exchange + merge over peer memory (one CTA per head): push this rank's partial of head h into
+// slot `rank` of every rank's buffer, publish a flag per (rank, head) after a system-scope fence,
+// wait for every rank's flag in the own buffer, then merge the world's partials in rank order.
+constexpr uint32_t kP2pPollLimit = 1u << 22;
+
+__global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __restrict__ part,
+                                                             const unsigned long long* __restrict__ peers, int world,
+                                                             int rank, int H, uint32_t tag, half* __restrict__ O,
+                                                             int* err) {
+    __shared__ float scratch[8 * kFdPart];
+    __shared__ float red[4];
+    const int h = blockIdx.x, d = threadIdx.x;
+    const size_t flag_off = (size_t)world * H * kFdPart;  // floats before the flags
+    const float* src = part + (size_t)h * kFdPart;
+    for (int p = 0; p < world; ++p) {
+        float* dst = reinterpret_cast<float*>(peers[p]) + ((size_t)rank * H + h) * kFdPart;
+        for (int i = d; i < kFdPart; i += kFdHeadDim) dst[i] = src[i];
+    }
+    __syncthreads();  // every thread's stores are issued before thread 0's fence
+    if (d == 0) {
+        __threadfence_system();  // the partial is visible at every rank before its flag
+        for (int p = 0; p < world; ++p) {
+            unsigned int* f = reinterpret_cast<unsigned int*>(reinterpret_cast<float*>(peers[p]) + flag_off);
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f + (size_t)rank * H + h), "r"(tag) : "memory");
+        }
+    }
+    float* own = reinterpret_cast<float*>(peers[rank]);
+    bool ok = true;
+    if (d < world) {
+        const unsigned int* f = reinterpret_cast<const unsigned int*>(own + flag_off) + (size_t)d * H + h;
+        ok = false;
+        for (uint32_t i = 0; i < kP2pPollLimit; ++i) {
+            unsigned int v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if (v == tag) { ok = true; break; }
+            if (i > 64) __nanosleep(64);
+        }
+    }
+    if (!__syncthreads_and(ok)) {
+        if (d == 0) atomicExch(err, 1);
+        return;
+    }
+    fd_merge_head(own + (size_t)h * kFdPart, world, H * kFdPart, scratch, 8 * kFdPart, red,
+                  O + (size_t)h * kFdHeadDim, nullptr);
+}
+
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -427,4 +474,49 @@ extern "C" int llmdiy_fd_mh_status(const float* work, int L, int num_heads) {
     cudaError_t e = cudaMemcpy(&h, work + (size_t)num_heads * S * kFdPart, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return (int)e;
     return h ? -5 : 0;
+}
+
+extern "C" size_t llmdiy_p2p_buffer_bytes(int world, int num_heads) {
+    if (world <= 0 || num_heads <= 0) return 0;
+    const size_t b = (size_t)world * num_heads * (kFdPart * sizeof(float) + sizeof(uint32_t));
+    return (b + 255) / 256 * 256;
+}
+
+extern "C" int llmdiy_p2p_alloc(size_t bytes, void** ptr, uint8_t* ipc_handle) {
+    if (!ptr || !ipc_handle || bytes == 0) return (int)cudaErrorInvalidValue;
+    *ptr = nullptr;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);  // flags start below every tag
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, *ptr);
+    if (e != cudaSuccess) {
+        if (*ptr) cudaFree(*ptr);
+        *ptr = nullptr;
+        return (int)e;
+    }
+    static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    return 0;
+}
+
+extern "C" int llmdiy_p2p_open(const uint8_t* ipc_handle, void** ptr) {
+    if (!ipc_handle || !ptr) return (int)cudaErrorInvalidValue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof(h));
+    return (int)cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+extern "C" int llmdiy_p2p_close(void* peer_ptr) { return (int)cudaIpcCloseMemHandle(peer_ptr); }
+
+extern "C" int llmdiy_p2p_free(void* ptr) { return (int)cudaFree(ptr); }
+
+extern "C" int llmdiy_fd_p2p_merge(const float* part, const uint64_t* peers, int world, int rank, int num_heads,
+                                   uint32_t tag, uint16_t* O, int* err, void* stream) {
+    if (!part || !peers || !O || !err || world <= 0 || world > kFdMergeMax || rank < 0 || rank >= world ||
+        num_heads <= 0 || tag == 0)
+        return (int)cudaErrorInvalidValue;
+    fd_p2p_merge_k<<<num_heads, kFdHeadDim, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        part, reinterpret_cast<const unsigned long long*>(peers), world, rank, num_heads, tag,
+        reinterpret_cast<half*>(O), err);
+    return (int)cudaGetLastError();
 }

@@ -79,6 +79,11 @@ def lib() -> ctypes.CDLL:
         "llmdiy_fd_mh_partials": [P, P, P, I, I, I, P, P, SZ, P],
         "llmdiy_fd_mh_merge": [P, I, I, P, P],
         "llmdiy_fd_mh_status": [P, I, I],
+        "llmdiy_p2p_alloc": [SZ, ctypes.POINTER(P), P],
+        "llmdiy_p2p_open": [P, ctypes.POINTER(P)],
+        "llmdiy_p2p_close": [P],
+        "llmdiy_p2p_free": [P],
+        "llmdiy_fd_p2p_merge": [P, P, I, I, I, ctypes.c_uint32, P, P, P],
         "llmdiy_argmax": [P, P, I, P],
         "llmdiy_hgemv": [P, P, P, I, I, P],
         "llmdiy_hgemm_swizzle_nn": [P, P, P, I, I, I, P],
@@ -112,6 +117,8 @@ def lib() -> ctypes.CDLL:
         fn = getattr(L, name)
         fn.argtypes = args
         fn.restype = ctypes.c_int
+    L.llmdiy_p2p_buffer_bytes.argtypes = [I, I]
+    L.llmdiy_p2p_buffer_bytes.restype = SZ
     L.llmdiy_engine_destroy.argtypes = [P]
     L.llmdiy_engine_destroy.restype = None
     L.llmdiy_engine_last_error.argtypes = [P]
@@ -227,6 +234,38 @@ def fd_mh_merge(parts, G, num_heads, O, stream=None):
 
 def fd_mh_status(work, L, num_heads):
     return lib().llmdiy_fd_mh_status(_p(work), L, num_heads)
+
+
+def p2p_buffer_bytes(world, num_heads):
+    return int(lib().llmdiy_p2p_buffer_bytes(world, num_heads))
+
+
+def p2p_alloc(nbytes):
+    """Device buffer for llmdiy_fd_p2p_merge: (pointer, 64-byte CUDA IPC handle)."""
+    ptr = ctypes.c_void_p()
+    h = (ctypes.c_uint8 * 64)()
+    _check(lib().llmdiy_p2p_alloc(nbytes, ctypes.byref(ptr), h), "p2p_alloc")
+    return ptr.value, bytes(h)
+
+
+def p2p_open(handle: bytes):
+    ptr = ctypes.c_void_p()
+    buf = (ctypes.c_uint8 * 64).from_buffer_copy(handle)
+    _check(lib().llmdiy_p2p_open(buf, ctypes.byref(ptr)), "p2p_open")
+    return ptr.value
+
+
+def p2p_close(ptr):
+    _check(lib().llmdiy_p2p_close(_p(ptr)), "p2p_close")
+
+
+def p2p_free(ptr):
+    _check(lib().llmdiy_p2p_free(_p(ptr)), "p2p_free")
+
+
+def fd_p2p_merge(part, peers, world, rank, num_heads, tag, O, err, stream=None):
+    _check(lib().llmdiy_fd_p2p_merge(_p(part), _p(peers), world, rank, num_heads, tag, _p(O), _p(err), _p(stream)),
+           "fd_p2p_merge")
 
 
 def argmax(out, logits, V, stream=None):

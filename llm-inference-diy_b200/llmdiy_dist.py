@@ -3,9 +3,11 @@
 The cache's positions are sharded contiguously over the ranks of a process group
 (one process per GPU).  Each rank computes one partial per head over its shard
 -- o[128] unnormalised, m (max score), l (sum of e^{s - m}) as 130 fp32 --
-with llmdiy_fd_mh_partials, the partials are all-gathered (NCCL over NVLink on
-GPUs), and every rank merges them in rank order with llmdiy_fd_mh_merge.  This
-is the only exchange on the path: 130 x num_heads fp32 per rank.
+with llmdiy_fd_mh_partials; then either the partials are all-gathered (NCCL over
+NVLink) and every rank merges them in rank order with llmdiy_fd_mh_merge, or one
+kernel per rank stores its partial straight into every rank's buffer over peer
+memory, raises flags and merges (P2PExchange, llmdiy_fd_p2p_merge).  This is the
+only exchange on the path: 130 x num_heads fp32 per rank.
 
 The reference has no multi-GPU path; its single-GPU counterpart is the per-head
 split-KV pair fd_v5_split_stage1 + fd_opt_stage2
@@ -41,6 +43,58 @@ def gather_partials(group, part, world: int, out=None):
     return out
 
 
+class P2PExchange:
+    """The partials exchange over peer memory (llmdiy_fd_p2p_merge): every rank allocates a receive
+    buffer, the ranks swap its CUDA IPC handle through the process group once, and each call is one
+    kernel per rank that stores the rank's partial into every buffer, raises flags and merges when
+    all ranks' flags are up.  Collective: every rank constructs it and calls it in the same order."""
+
+    def __init__(self, group, num_heads: int, device):
+        import torch
+        import torch.distributed as dist
+        import llmdiy_b200 as L
+        self.world = dist.get_world_size(group) if group is not None else 1
+        self.rank = dist.get_rank(group) if group is not None else 0
+        self.num_heads = num_heads
+        self.own, handle = L.p2p_alloc(L.p2p_buffer_bytes(self.world, num_heads))
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle, group=group)
+        else:
+            handles = [handle]
+        self.opened = []
+        ptrs = []
+        for r in range(self.world):
+            if r == self.rank:
+                ptrs.append(self.own)
+            else:
+                p = L.p2p_open(handles[r])
+                self.opened.append(p)
+                ptrs.append(p)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.tag = 0
+
+    def __call__(self, part, out, stream):
+        import llmdiy_b200 as L
+        self.tag += 1
+        L.fd_p2p_merge(part.data_ptr(), self.peers.data_ptr(), self.world, self.rank, self.num_heads, self.tag,
+                       out.data_ptr(), self.err.data_ptr(), stream=stream)
+
+    def status(self) -> int:
+        """0, or 1 when a wait for another rank's flags expired (after synchronising)."""
+        return int(self.err.item())
+
+    def close(self):
+        import llmdiy_b200 as L
+        for p in self.opened:
+            L.p2p_close(p)
+        self.opened = []
+        if self.own:
+            L.p2p_free(self.own)
+            self.own = 0
+
+
 class SplitKVAttention:
     """Distributed decode attention over a sharded cache.
 
@@ -50,7 +104,9 @@ class SplitKVAttention:
     exercise the sharding and exchange logic on gloo ranks.
     """
 
-    def __init__(self, group, num_heads: int, stride: int, partials=None, merge=None):
+    def __init__(self, group, num_heads: int, stride: int, partials=None, merge=None, exchange: str = "nccl"):
+        """exchange: "nccl" (all-gather of the partials, then a merge kernel) or "p2p" (one kernel per
+        rank that exchanges over peer memory and merges: P2PExchange; CUDA devices only)."""
         import torch.distributed as dist
         self.group = group
         self.world = dist.get_world_size(group) if group is not None else 1
@@ -59,6 +115,10 @@ class SplitKVAttention:
         self.stride = stride
         self._partials = partials or self._gpu_partials
         self._merge = merge or self._gpu_merge
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(exchange)
+        self.exchange = exchange
+        self._p2p = None
         self._work = None
         self._bufs = None  # (part, parts) reused across calls on one device
 
@@ -75,9 +135,19 @@ class SplitKVAttention:
                           torch.empty((self.world, self.num_heads, PART), dtype=torch.float32, device=q.device))
         part, parts = self._bufs
         self._partials(q, K_shard, V_shard, r1 - r0, part)
+        if self.exchange == "p2p":
+            if self._p2p is None:
+                self._p2p = P2PExchange(self.group, self.num_heads, q.device)
+            self._p2p(part, out, torch.cuda.current_stream(q.device).cuda_stream)
+            return out
         gather_partials(self.group, part, self.world, parts)
         self._merge(parts, out)
         return out
+
+    def close(self):
+        if self._p2p is not None:
+            self._p2p.close()
+            self._p2p = None
 
     # ---- default implementations: the sm_100a kernels
     def _gpu_partials(self, q, K, V, rows, part):

@@ -116,3 +116,32 @@ def test_fd_multihead_rejects_bad_arguments(rng):
         L.fd_multihead(p + 2, p, p, p, 16, 2048, 16, w.data_ptr(), 1 << 18)  # misaligned q
     with pytest.raises(L.LlmdiyError):
         L.fd_multihead(p, p, p, p, 16, 2048, 16, w.data_ptr(), 4)  # workspace too small
+
+
+def test_fd_p2p_exchange_single_rank(oracle, rng):
+    """The peer-memory exchange kernel (llmdiy_fd_p2p_merge) with one rank on one GPU: the partial
+    goes through the rank's own IPC-exported buffer and flag, and the merge equals the attention
+    over the shard; later calls (new tags) reuse the buffer.  The multi-rank run is the 2-GPU
+    `bench.py --workload fd-op`, which checks it against the NCCL all-gather path."""
+    import llmdiy_dist as D
+    t = torch()
+    H, stride, n = 16, 2048, 3000
+    ex = D.P2PExchange(None, H, t.device("cuda"))
+    try:
+        for call in range(3):
+            q, K, V = _inputs(rng, n, H, stride)
+            dq, dK, dV = dev(q), dev(K), dev(V)
+            part = t.zeros((H, 130), dtype=t.float32, device="cuda")
+            w, nb = _work(n, H)
+            L.fd_mh_partials(dq.data_ptr(), dK.data_ptr(), dV.data_ptr(), n, stride, H, part.data_ptr(),
+                             w.data_ptr(), nb)
+            O = zeros16(H * 128)
+            ex(part, O, None)
+            t.cuda.synchronize()
+            assert ex.status() == 0 and ex.tag == call + 1
+            got = host(O).reshape(H, 128)
+            for h in (0, 7, H - 1):
+                exp = oracle.attention_q1(q[h * 128:(h + 1) * 128], K[h * 128:], V[h * 128:], n, stride)
+                assert max_abs(got[h], exp) < 1e-3, (call, h)
+    finally:
+        ex.close()
