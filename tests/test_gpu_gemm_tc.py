@@ -12,8 +12,12 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 384, 2048), (200, 136, 5504), (1, 128, 64),
-                                   (127, 6144, 2048), (2048, 2048, 2048), (333, 11008, 2048), (2048, 2048, 5504)])
+                                   (127, 6144, 2048), (2048, 2048, 2048), (333, 11008, 2048), (2048, 2048, 5504),
+                                   (2048, 6144, 2048), (1000, 4736, 320)])
 def test_gemm_tc(rng, M, N, K):
+    """M > 128 with at least as many 256 x 256 tiles as SM pairs takes the persistent 2-CTA kernel
+    (several tiles per pair, ragged M and N edges, K shorter than its pipeline); the rest the
+    single-SM kernel."""
     A = (rng.standard_normal((M, K)) * 0.5).astype(np.float16)
     W = (rng.standard_normal((N, K)) * (1.0 / np.sqrt(K))).astype(np.float16)
     dA, dW, C = dev(A), dev(W), zeros16(M * N)  # keep the inputs alive during the call
