@@ -112,7 +112,7 @@ struct DecodeArgs {
     // %globaltimer at arrival and at release; per CTA the producer's time
     // blocked on a full ring and the consumers' time waiting for data.
     unsigned long long* prof;       // [grid][prof_cap][2]
-    unsigned long long* prof_prod;  // [grid][2]
+    unsigned long long* prof_prod;  // [grid][6 phases][8 warps][4]: wait, compute, issue cycles, longest wait
     int prof_cap;
 };
 

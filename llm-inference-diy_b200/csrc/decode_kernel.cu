@@ -452,8 +452,8 @@ __device__ __forceinline__ void gemv_phase(int PH, const DecodeArgs& a, Smem& s,
                                            uint64_t pol) {
     const int R = PH == PH_LM ? 4 : PH == PH_C ? 3 : PH == PH_W12 ? 2 : PH == PH_O ? 1 : 0;
     const int u0 = s.range[R][0], u1 = s.range[R][1], CH = s.range[R][2], K = s.range[R][3];
-    unsigned long long pw = 0, pc = 0, pi = 0, pn = 0;  // probe sums (profiling only)
-    unsigned long long pmaxw = 0;  // DEBUG: longest single wait
+    unsigned long long pw = 0, pc = 0, pi = 0;  // per-chunk cycle sums (profiling only)
+    unsigned long long pmaxw = 0;  // longest single chunk wait (profiling only)
     for (int cu = u0; cu < u1; cu += CH, ++chunk) {
         if ((int)(chunk & (kRingStages - 1)) != warp) continue;
         const int nun = (u1 - cu) < CH ? (u1 - cu) : CH;
@@ -508,16 +508,15 @@ __device__ __forceinline__ void gemv_phase(int PH, const DecodeArgs& a, Smem& s,
             pmaxw = (t1 - t0) > pmaxw ? (t1 - t0) : pmaxw;
             pc += t2 - t1;
             pi += (unsigned long long)clock64() - t2;
-            pn += 1;
         }
     }
     if (a.prof_prod && lane == 0) {
-        // per CTA, phase and warp: SM cycles waiting for chunks, computing, issuing; chunks
+        // per CTA, phase and warp: SM cycles waiting for chunks, computing, issuing; the longest wait
         unsigned long long* q = a.prof_prod + (((size_t)blockIdx.x * 6 + PH) * kConsumerWarps + warp) * 4;
         atomicAdd(q, pw);  // reductions: no round trip on the phase's critical path
         atomicAdd(q + 1, pc);
         atomicAdd(q + 2, pi);
-        atomicMax(q + 3, pmaxw);  // DEBUG: longest single wait
+        atomicMax(q + 3, pmaxw);
     }
 }
 

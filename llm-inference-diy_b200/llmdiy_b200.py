@@ -427,7 +427,10 @@ class Engine:
         return k.view(np.float16), v.view(np.float16)
 
     def profile(self, first_token: int, pos: int, n_steps: int, cap: int = 4096):
-        """Timing probes of one decode launch: (barrier ns [cta, cap, 2], producer/consumer stall ns [cta, 2])."""
+        """Timing probes of one decode launch (development aid): (probe times [cta, cap, 2] in
+        %globaltimer ns -- per CTA and phase boundary, warp 0's and the last warp's arrival -- and
+        per-chunk accounting [cta, 6 phases, 8 warps, 4] in SM cycles: chunk wait, compute, refill
+        issue, longest single wait)."""
         import numpy as np
         G = self.num_sms
         out = np.zeros((G, cap, 2), dtype=np.uint64)
