@@ -40,7 +40,7 @@ namespace {
 
 constexpr int kBatchMax = 64;
 constexpr int kBRows = 64;   // KV rows per TMA tile
-constexpr int kBSplitRows = 1024;  // KV rows per attention work item
+constexpr int kBSplitRows = 4096;  // KV rows per attention work item (each boundary costs a partial write)
 constexpr int kBStages = 6;
 constexpr int kBPart = kHeadDim + 2;
 
@@ -139,8 +139,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_k(const float* __restrict__
 }
 
 // ---------------------------------------------------------------- ragged split-KV attention
-// Work items are (sequence b, head h, split sp) over rows [sp*1024, min(len, (sp+1)*1024)).
-// Longest first: every full 1024-row split (16 tiles) is numbered before the partial last
+// Work items are (sequence b, head h, split sp) over rows [sp*S, min(len, (sp+1)*S)), S = kBSplitRows.
+// Longest first: every full split (S / 64 tiles) is numbered before the partial last
 // splits, which follow in decreasing size.  CTAs claim items from a per-layer counter
 // (zeroed at the start of each step) as their producer thread needs them, so a CTA that
 // drew short items simply takes more: the grid finishes together.
