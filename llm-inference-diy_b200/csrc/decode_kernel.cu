@@ -12,7 +12,7 @@
 // (fp32 FMA dot products against the activation held in registers or shared
 // memory), with the reference's small ops fused into the epilogues:
 //   QKV  : RMSNorm(ln_1) prologue; bias; RoPE; K/V append at row pos
-//   ATT  : 16 heads x 9 position splits; the last CTA of a head merges (m,l,o)
+//   ATT  : 16 heads x 9 position splits; split 0 of a head merges the (m,l,o) partials
 //   O    : residual add
 //   W12  : RMSNorm(ln_2) prologue; SwiGLU (silu on the w2 output)
 //   C    : residual add
