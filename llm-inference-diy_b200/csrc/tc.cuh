@@ -107,8 +107,4 @@ LLMDIY_DEV void tmem_st16(uint32_t taddr, const uint32_t* r) {
 }
 LLMDIY_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Shared-memory writes by threads (generic proxy) become visible to the tensor core's operand
-// reads (async proxy) once followed by this fence and a synchronisation with the MMA issuer.
-LLMDIY_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
 }  // namespace llmdiy
