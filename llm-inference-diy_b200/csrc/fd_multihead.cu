@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_merge_ranks_k(const float* __re
 // Exchange + merge over peer memory (one CTA per head): push this rank's partial of head h into
 // slot `rank` of every rank's buffer, publish a flag per (rank, head) after a system-scope fence,
 // wait for every rank's flag in the own buffer, then merge the world's partials in rank order.
-constexpr uint32_t kP2pPollLimit = 1u << 22;
+constexpr uint32_t kP2pPollLimit = 1u << 20;  // about a second of polling
 
 __global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __restrict__ part,
                                                              const unsigned long long* __restrict__ peers, int world,

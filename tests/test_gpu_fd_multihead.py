@@ -145,3 +145,36 @@ def test_fd_p2p_exchange_single_rank(oracle, rng):
                 assert max_abs(got[h], exp) < 1e-3, (call, h)
     finally:
         ex.close()
+
+
+def test_fd_p2p_wait_expires_without_a_peer():
+    """Failure detection without a GPU fault: a rank of a two-rank exchange whose peer never runs.
+    The partner's buffer is a second local buffer that nothing writes flags into, so the kernel's
+    bounded wait for rank 1 runs out; the kernel reports it in the error word and returns, and the
+    context stays usable for a normal call afterwards."""
+    import time
+    t = torch()
+    H = 16
+    nb = L.p2p_buffer_bytes(2, H)
+    own, _ = L.p2p_alloc(nb)
+    other, _ = L.p2p_alloc(nb)
+    try:
+        peers = t.tensor([own, other], dtype=t.int64, device="cuda")
+        part = t.zeros((H, 130), dtype=t.float32, device="cuda")
+        part[:, 129] = 1.0
+        O = zeros16(H * 128)
+        err = t.zeros(1, dtype=t.int32, device="cuda")
+        t0 = time.time()
+        L.fd_p2p_merge(part.data_ptr(), peers.data_ptr(), 2, 0, H, 1, O.data_ptr(), err.data_ptr())
+        t.cuda.synchronize()
+        assert int(err.item()) == 1
+        assert time.time() - t0 < 60
+        # the same buffer as a one-rank exchange afterwards: completes normally
+        err.zero_()
+        one = t.tensor([own], dtype=t.int64, device="cuda")
+        L.fd_p2p_merge(part.data_ptr(), one.data_ptr(), 1, 0, H, 2, O.data_ptr(), err.data_ptr())
+        t.cuda.synchronize()
+        assert int(err.item()) == 0
+    finally:
+        L.p2p_free(own)
+        L.p2p_free(other)
