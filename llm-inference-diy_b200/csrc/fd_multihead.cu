@@ -9,7 +9,8 @@
 // state per half-warp, and writes its unnormalised partial (o[128], m, l) in
 // fp32.  A second kernel merges each head's partials (log-sum-exp) into the
 // fp16 output or into one fp32 partial per head — the form the multi-GPU path
-// exchanges (NCCL all-gather) before the final merge of the shards' partials.
+// exchanges (over peer memory with fd_p2p_merge_k, or by an NCCL all-gather)
+// before the final merge of the shards' partials.
 #include <cuda.h>
 #include <algorithm>
 #include <cstring>
