@@ -23,6 +23,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -106,6 +107,222 @@ struct EpiStoreRows {
         *reinterpret_cast<uint4*>(d + 8) = pack8(v + 8);
     }
 };
+
+// ---------------------------------------------------------------- weight-row GEMM for M = B <= 64
+// C[B, N] = X[B, K] W[N, K]^T with the weights as the MMA's M side: a tile is 128 rows of W
+// (128 output columns) against all B <= 64 activation rows (MMA N = 64; rows past B are zero-filled
+// by TMA), so the weights stream exactly once.  K is split over the z CTAs of a thread-block
+// cluster (z = 1..8, chosen on the host): CTA r of a cluster accumulates k-blocks
+// [r*per, (r+1)*per) of the cluster's tiles in TMEM, and the z fp32 partial tiles are summed
+// through distributed shared memory — no partial sums in HBM and no separate reduce launch.
+// Persistent: cluster p of P takes tiles p, p + P, ...
+// Roles: warp 0 loads (W 16 KB + X 8 KB per 64-wide k-block, 6 stages), warp 1 issues the MMAs
+// into one of two 64-column TMEM accumulators, warps 2-5 copy a finished accumulator into shared
+// memory in [row][column] order, then each CTA of the cluster sums its share of the 16-column
+// groups over the z copies (in rank order) and applies the epilogue op the split-K path uses.
+// Cluster handshakes are mbarriers: `ready` (every CTA's copy of tile i is in place) and `freed`
+// (every CTA has read this CTA's copy of tile i); all waits are bounded.
+constexpr int kWrStages = 6;
+constexpr int kWrThreads = 192;
+constexpr int kWrMaxSplit = 8;
+
+struct WrSmem {
+    half w[kWrStages][128 * kGemmBK];  // 16 KB per stage
+    half x[kWrStages][64 * kGemmBK];   // 8 KB per stage
+    float t[64][128 + 4];              // this CTA's partial tile, [row][column] (padded rows)
+    uint64_t full[kWrStages], empty[kWrStages], acc_full[2], acc_empty[2];
+    uint64_t ready;  // z arrivals per tile: every CTA's partial tile is written
+    uint64_t freed;  // z arrivals per tile: every CTA has finished reading this CTA's partial
+    uint32_t tmem_base;
+    int fail;
+};
+
+LLMDIY_DEV uint32_t wr_cluster_reg(int which) {
+    uint32_t r;
+    if (which == 0) asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    else asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+LLMDIY_DEV uint32_t wr_mapa(const void* p, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
+    return d;
+}
+LLMDIY_DEV void wr_arrive_remote(uint32_t bar_cluster) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// Bounded wait with cluster-scope acquire (the arrivals come from other CTAs of the cluster).
+LLMDIY_DEV bool wr_wait_cluster(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n"
+            " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if (*abort_flag) return false;
+        if (i > 64) __nanosleep(64);
+    }
+    return false;
+}
+LLMDIY_DEV float4 wr_ld_cluster(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+LLMDIY_DEV void wr_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <class Epi>
+__global__ void __launch_bounds__(kWrThreads, 1)
+    gemm_wrows_k(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, int B, int N, int K,
+                 Epi epi, int* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    WrSmem& s = *reinterpret_cast<WrSmem*>(smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r = (int)wr_cluster_reg(0), z = (int)wr_cluster_reg(1);
+    const int p0 = (int)blockIdx.x / z, P = (int)gridDim.x / z;
+    const int T = (N + 127) / 128, KB = (K + kGemmBK - 1) / kGemmBK;
+    const int per = (KB + z - 1) / z, kb0 = r * per, kb1 = min(KB, kb0 + per);  // host: kb0 < kb1
+    constexpr uint32_t kCols = 128;  // two 64-column accumulators
+    if (tid == 0) {
+        for (int i = 0; i < kWrStages; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s.acc_full[i], 1);
+            mbar_init(&s.acc_empty[i], 128);
+        }
+        mbar_init(&s.ready, (uint32_t)z);
+        mbar_init(&s.freed, (uint32_t)z);
+        s.fail = 0;
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&s.tmem_base, kCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    wr_cluster_sync();  // barriers initialised in every CTA before any remote arrive
+    tc_fence_after();
+    const uint32_t tmem = s.tmem_base;
+    if (warp == 0) {
+        if (lane == 0) {
+            int g = 0;
+            for (int t = p0; t < T && !s.fail; t += P) {
+                for (int kb = kb0; kb < kb1; ++kb, ++g) {
+                    const int st = g % kWrStages;
+                    if (g >= kWrStages && !mbar_wait(&s.empty[st], ((g / kWrStages) - 1) & 1, &s.fail)) {
+                        s.fail = 1;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&s.full[st], (128 + 64) * kGemmBK * 2);
+                    tma_load_2d(s.w[st], &tw, kb * kGemmBK, t * 128, &s.full[st]);
+                    tma_load_2d(s.x[st], &tx, kb * kGemmBK, 0, &s.full[st]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_f16_f32(128, 64, false);
+            int g = 0, it = 0;
+            bool ok = true;
+            for (int t = p0; ok && t < T; t += P, ++it) {
+                const int buf = it & 1;
+                if (it >= 2 && !mbar_wait(&s.acc_empty[buf], ((it >> 1) - 1) & 1, &s.fail)) { ok = false; break; }
+                tc_fence_after();
+                for (int kb = kb0; kb < kb1; ++kb, ++g) {
+                    const int st = g % kWrStages;
+                    if (!mbar_wait(&s.full[st], (g / kWrStages) & 1, &s.fail)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t w0 = smem_u32(s.w[st]), x0 = smem_u32(s.x[st]);
+#pragma unroll
+                    for (int k = 0; k < kGemmBK / 16; ++k)
+                        umma_f16(tmem + 64u * buf, umma_desc_sw128(w0 + 32 * k), umma_desc_sw128(x0 + 32 * k), idesc,
+                                 (kb > kb0 || k > 0) ? 1u : 0u);
+                    umma_commit(&s.empty[st]);
+                }
+                if (ok) umma_commit(&s.acc_full[buf]);
+            }
+            if (!ok) s.fail = 1;
+        }
+    } else {
+        const int q = warp & 3, et = tid - 64;  // epilogue thread 0..127
+        int it = 0;
+        for (int t = p0; t < T; t += P, ++it) {
+            const int buf = it & 1;
+            bool ok = mbar_wait(&s.acc_full[buf], (it >> 1) & 1, &s.fail);
+            // every CTA has read this CTA's partial of the previous tile before it is overwritten
+            if (ok && it > 0) ok = wr_wait_cluster(&s.freed, (it - 1) & 1, &s.fail);
+            if (named_bar_or(1, 128, !ok)) {
+                s.fail = 1;
+                break;
+            }
+            tc_fence_after();
+            // TMEM lane 32q + lane = tile column 32q + lane; TMEM columns = the B rows
+            const uint32_t a = tmem + 64u * buf + ((uint32_t)(q * 32) << 16);
+#pragma unroll
+            for (int c = 0; c < 64; c += 16) {
+                uint32_t v[16];
+                tmem_ld16(a + c, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) s.t[c + e][q * 32 + lane] = __uint_as_float(v[e]);
+            }
+            tc_fence_before();
+            mbar_arrive(&s.acc_empty[buf]);  // the accumulator may take tile it+2
+            named_bar_sync(1, 128);          // this CTA's partial tile is complete
+            if (et == 0) {
+                asm volatile("fence.acq_rel.cluster;" ::: "memory");
+                for (int j = 0; j < z; ++j) wr_arrive_remote(wr_mapa(&s.ready, (uint32_t)j));
+            }
+            if (named_bar_or(1, 128, !wr_wait_cluster(&s.ready, it & 1, &s.fail))) {
+                s.fail = 1;
+                break;
+            }
+            // this CTA's share of the tile's B x 8 groups of 16 columns, summed over ranks 0..z-1
+            const int n0 = t * 128;
+            for (int i = r + z * et; i < B * 8; i += z * 128) {
+                const int row = i >> 3, c = (i & 7) * 16, n = n0 + c;
+                if (n >= N) continue;
+                float acc[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+                const uint32_t off = smem_u32(&s.t[row][c]);
+                for (int j = 0; j < z; ++j) {
+                    const uint32_t src = wr_mapa(&s.t[0][0], (uint32_t)j) + (off - smem_u32(&s.t[0][0]));
+#pragma unroll
+                    for (int e = 0; e < 16; e += 4) {
+                        const float4 f = wr_ld_cluster(src + 4u * e);
+                        acc[e] += f.x;
+                        acc[e + 1] += f.y;
+                        acc[e + 2] += f.z;
+                        acc[e + 3] += f.w;
+                    }
+                }
+                epi(row, n, acc);
+            }
+            named_bar_sync(1, 128);  // this CTA's reads of every partial are done
+            if (et == 0)
+                for (int j = 0; j < z; ++j) wr_arrive_remote(wr_mapa(&s.freed, (uint32_t)j));
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && s.fail) atomicExch(err, 1);
+    // no CTA leaves while a peer may still read its partial tile or arrive on its barriers
+    wr_cluster_sync();
+    if (warp == 0) tmem_dealloc(tmem, kCols);
+}
 
 // Sum the split-K slices of one (row, 16 columns) in slice order and apply `epi`.
 // Four threads share a 16-column group (4 columns each, one float4 load per
@@ -466,6 +683,8 @@ struct llmdiy_batch {
     float* fdp = nullptr;
     int *tok = nullptr, *pos = nullptr, *next = nullptr, *hist = nullptr, *step = nullptr, *err = nullptr;
     int* ctr = nullptr;  // [num_layers] attention work counters
+    bool wrows = false;  // weight-row GEMMs (env LLMDIY_BATCH_WROWS=1) instead of split-K + reduce
+    int wr_fit[kWrMaxSplit + 1] = {};  // clusters of each size the weight-row GEMM fits at once
     int hist_steps = 0;
     half* pf = nullptr;  // prefill scratch (kPrefillChunk rows)
     std::vector<CUtensorMap> kmaps, vmaps;  // per layer, over [max_batch * max_len][H]
@@ -495,9 +714,84 @@ int ksplit_for(int N, int K, int sms) {
     return (KB + per - 1) / per;
 }
 
+// Cluster size z and number of clusters P for the weight-row GEMM: the fewest k-blocks on the
+// busiest CTA (ceil(T / P) tiles x ceil(KB / z) blocks), P capped by the clusters of size z that
+// fit on the device at once (cached in fit[z]); ties go to the smaller z.  Every rank's k-range
+// is non-empty.
+void wrows_split(const int* fit, int T, int KB, int* z_out, int* P_out) {
+    int bz = 1, bP = std::max(1, std::min(T, fit[1])), best = ((T + bP - 1) / bP) * KB;
+    for (int z = 2; z <= kWrMaxSplit; ++z) {
+        const int per = (KB + z - 1) / z;
+        if (fit[z] < 1 || (KB + per - 1) / per != z) continue;
+        const int P = std::min(T, fit[z]), cost = ((T + P - 1) / P) * per;
+        if (cost < best) best = cost, bz = z, bP = P;
+    }
+    *z_out = bz;
+    *P_out = bP;
+}
+
+// The weight-row GEMM above for M = B <= 64 (N a multiple of 16, K of 8, rows 16-byte aligned).
+template <class Epi>
+int gemm_wrows(llmdiy_batch* b, const half* A, int lda, const half* W, int N, int K, int M, const Epi& epi,
+               cudaStream_t st) {
+    CUtensorMap tw, tx;
+    if (M < 1 || M > 64 || !make_kmajor_map(&tw, W, N, K, K, 128) || !make_kmajor_map(&tx, A, M, K, lda, 64))
+        return (int)cudaErrorInvalidValue;
+    int* err = gemm_err_word();
+    if (!err) return (int)cudaErrorMemoryAllocation;
+    auto kern = gemm_wrows_k<Epi>;
+    static std::once_flag attr;
+    std::call_once(attr, [&] {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(WrSmem));
+    });
+    int z = 1, P = 1;
+    wrows_split(b->wr_fit, (N + 127) / 128, (K + kGemmBK - 1) / kGemmBK, &z, &P);
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)(z * P));
+    lc.blockDim = dim3(kWrThreads);
+    lc.dynamicSmemBytes = sizeof(WrSmem);
+    lc.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = (unsigned)z;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&lc, kern, tw, tx, M, N, K, epi, err);
+}
+
+// Clusters of each size 1..8 that the weight-row GEMM fits on the device at once (0 = none).
+void wrows_fit(int* fit, int sms) {
+    auto kern = gemm_wrows_k<EpiStoreRows>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(WrSmem));
+    fit[0] = 0;
+    fit[1] = sms;
+    for (int z = 2; z <= kWrMaxSplit; ++z) {
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3((unsigned)(z * 64));
+        lc.blockDim = dim3(kWrThreads);
+        lc.dynamicSmemBytes = sizeof(WrSmem);
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)z;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        lc.attrs = at;
+        lc.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &lc) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        fit[z] = n;
+    }
+}
+
 template <class Epi>
 int gemm_rows(llmdiy_batch* b, const half* A, int lda, const half* W, int N, int K, int M, const Epi& epi,
               cudaStream_t st) {
+    if (b->wrows) return gemm_wrows(b, A, lda, W, N, K, M, epi, st);
     const int z = ksplit_for(N, K, b->v.num_sms);
     if (z == 1) return launch_gemm_tc(A, lda, W, K, M, N, K, epi, st);
     if ((size_t)z * M * N > b->ws_floats) return (int)cudaErrorInvalidValue;
@@ -561,6 +855,7 @@ int llmdiy_batch_create(llmdiy_engine* e, int max_batch, int max_len, llmdiy_bat
     BCK(cudaSetDevice(b->v.device), "cudaSetDevice");
     b->Bmax = max_batch;
     b->max_len = max_len;
+    if (const char* wr = std::getenv("LLMDIY_BATCH_WROWS")) b->wrows = wr[0] == '1';
     b->Smax = (max_len + kBSplitRows - 1) / kBSplitRows;
     const size_t H = kHidden, IM = c.intermediate_size, V = c.vocab_size, NL = c.num_layers;
     b->layer_stride = (size_t)max_batch * max_len * H;
@@ -585,6 +880,7 @@ int llmdiy_batch_create(llmdiy_engine* e, int max_batch, int max_len, llmdiy_bat
     for (auto& sh : shapes) wsf = std::max(wsf, (size_t)ksplit_for(sh[0], sh[1], sms) * max_batch * sh[0]);
     wsf = std::max(wsf, (size_t)ksplit_for((int)V, kHidden, sms) * max_batch * V);
     b->ws_floats = wsf;
+    if (b->wrows) wrows_fit(b->wr_fit, sms);
     alloc((void**)&b->ws, wsf * 4, "split-K workspace");
     alloc((void**)&b->fdp, (size_t)max_batch * kHeads * b->Smax * kBPart * 4, "attention partials");
     alloc((void**)&b->tok, kBatchMax * 4, "tokens");
@@ -618,9 +914,13 @@ int llmdiy_batch_create(llmdiy_engine* e, int max_batch, int max_len, llmdiy_bat
         if (ce != cudaSuccess) rc = bfail(b, (int)ce, "smem attribute");
     }
     if (!rc) {
+        // cudaMemset runs on the legacy stream, which does not order against the engine's
+        // non-blocking stream (fill_random, prefill and decode run there or on a caller's
+        // stream): the device sync keeps a slow clear from landing on rows written afterwards
         cudaError_t ce = cudaMemset(b->kc, 0, NL * b->layer_stride * 2);
         if (ce == cudaSuccess) ce = cudaMemset(b->vc, 0, NL * b->layer_stride * 2);
         if (ce == cudaSuccess) ce = cudaMemset(b->err, 0, 4);
+        if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
         if (ce != cudaSuccess) rc = bfail(b, (int)ce, "clear caches");
     }
     if (rc) {
@@ -666,7 +966,9 @@ int llmdiy_batch_prefill(llmdiy_batch* b, int seq, const int* tokens, int n) {
     BCK(cudaSetDevice(b->v.device), "cudaSetDevice");
     int* dtok = nullptr;
     BCK(cudaMalloc(&dtok, sizeof(int) * n), "prompt buffer");
-    cudaError_t ce = cudaMemcpy(dtok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice);
+    // on the prefill's own stream (a plain cudaMemcpy from pageable memory may return before
+    // its DMA lands, and the legacy stream does not order against the non-blocking one)
+    cudaError_t ce = cudaMemcpyAsync(dtok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, b->v.stream);
     const size_t H = kHidden, R = kPrefillChunk;
     PrefillArgs p{};
     p.layers = b->v.layers;

@@ -312,8 +312,12 @@ int create_common(llmdiy_engine* e, Source& src) {
     if (const char* v = std::getenv("LLMDIY_L2_AHEAD")) e->l2_ahead = std::max(0, std::atoi(v));
     int rc = load_weights(e, src);
     if (!rc) rc = build_feed_table(e);
+    if (!rc) rc = alloc_state(e);
     if (rc) return rc;
-    return alloc_state(e);
+    // the uploads and clears above ran on the legacy stream, which does not order against the
+    // engine's non-blocking stream or a caller's stream: finish them before any launch
+    CK(cudaDeviceSynchronize(), "finish set-up");
+    return LLMDIY_OK;
 }
 
 // Launch the decode kernel for n_steps steps (first input token, first position).
@@ -644,8 +648,8 @@ int llmdiy_engine_profile(llmdiy_engine* e, int first_token, int pos, int n_step
     CK(cudaMalloc(&d, n * 8), "alloc probes");
     const size_t np = (size_t)e->num_sms * 6 * kConsumerWarps * 4;
     CK(cudaMalloc(&dp, np * 8), "alloc probes");
-    cudaMemset(d, 0, n * 8);
-    cudaMemset(dp, 0, np * 8);
+    cudaMemsetAsync(d, 0, n * 8, e->stream);
+    cudaMemsetAsync(dp, 0, np * 8, e->stream);
     int rc = launch(e, first_token, pos, n_steps, false, false, false, e->stream, d, dp, cap);
     if (!rc) {
         cudaError_t c = cudaStreamSynchronize(e->stream);

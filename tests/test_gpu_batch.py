@@ -99,3 +99,30 @@ def test_batch_rejects_bad_arguments(engine):
     b.close()
     with pytest.raises(L.LlmdiyError):
         L.Batch(engine, max_batch=65, max_len=16)
+
+
+def test_batch_weight_row_gemms_match_splitk_at_64(engine, monkeypatch):
+    """The step's GEMMs at the full batch of 64 rows: the weight-row GEMMs (K split over a
+    thread-block cluster, partials summed in shared memory; LLMDIY_BATCH_WROWS=1) against the
+    split-K path (per-slice partials in HBM and a reduce launch) on the same caches
+    and tokens.  Both accumulate in fp32; logits within 2e-2, greedy tokens equal except
+    where the two logits' top-2 are within that tolerance."""
+    rng = np.random.default_rng(47)
+    B, steps = 64, 1
+    lens = rng.integers(1, 300, B).tolist()
+    toks = rng.integers(0, SMALL["vocab_size"], B).tolist()
+    out = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("LLMDIY_BATCH_WROWS", mode)
+        b = L.Batch(engine, max_batch=B, max_len=320)
+        for s in range(B):
+            b.fill_random(s, lens[s], seed=500 + s)
+        t = b.decode(toks, lens, steps)
+        out[mode] = (t, np.stack([b.logits(s).astype(np.float32) for s in range(B)]))
+        b.close()
+    (t0, l0), (t1, l1) = out["0"], out["1"]
+    assert float(np.max(np.abs(l0 - l1))) < 2e-2
+    for s in range(B):
+        if t0[-1, s] != t1[-1, s]:
+            top = np.sort(l1[s])[-2:]
+            assert top[1] - top[0] < 2e-2, s
