@@ -205,6 +205,9 @@ __global__ void __launch_bounds__(kWrThreads, 1)
         mbar_init(&s.freed, (uint32_t)z);
         s.fail = 0;
         mbar_fence_init();
+        // the first weight blocks of the first tile into L2 before pdl_wait (weights are constant)
+        if (p0 < T)
+            for (int kb = kb0; kb < kb1 && kb < kb0 + kGemmPrefetchBlocks; ++kb) tma_prefetch_2d(&tw, kb * kGemmBK, p0 * 128);
     }
     if (warp == 0) {
         tmem_alloc(&s.tmem_base, kCols);
@@ -214,6 +217,8 @@ __global__ void __launch_bounds__(kWrThreads, 1)
     wr_cluster_sync();  // barriers initialised in every CTA before any remote arrive
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
+    pdl_wait();  // X and the epilogue's outputs depend on earlier kernels
+    pdl_launch_dependents();
     if (warp == 0) {
         if (lane == 0) {
             int g = 0;
@@ -329,6 +334,8 @@ __global__ void __launch_bounds__(kWrThreads, 1)
 // slice), then lane 4k of the quad gathers the 16 sums and runs the op.
 template <class Epi>
 __global__ void __launch_bounds__(256) splitk_reduce_k(const float* __restrict__ ws, int Z, int M, int N, Epi epi) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int groups = N / 16;
     const int gidx = (blockIdx.x * blockDim.x + threadIdx.x) >> 2, part = threadIdx.x & 3;
     const bool live = gidx < M * groups;  // the quad is warp-aligned: all four lanes agree
@@ -414,6 +421,8 @@ __global__ void __launch_bounds__(128, 1)
     BFdSmem& s = *reinterpret_cast<BFdSmem*>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hw = lane >> 4, dl = (lane & 15) * 8;
     const uint64_t pol = l2_policy_evict_first();
+    pdl_wait();
+    pdl_launch_dependents();
     if (tid < B) s.len[tid] = pos[tid] + 1;
     __syncthreads();
     if (tid < B) {
@@ -576,6 +585,8 @@ __global__ void __launch_bounds__(128, 1)
 __global__ void __launch_bounds__(kHeadDim) bfd_merge_k(const float* __restrict__ part, const int* __restrict__ pos,
                                                         int Smax, half* __restrict__ att) {
     const int b = blockIdx.x / kHeads, h = blockIdx.x % kHeads, d = threadIdx.x;
+    pdl_wait();
+    pdl_launch_dependents();
     const int S = (pos[b] + 1 + kBSplitRows - 1) / kBSplitRows;
     const float* p = part + (size_t)(b * kHeads + h) * Smax * kBPart;
     float M = -INFINITY;
@@ -595,6 +606,8 @@ __global__ void __launch_bounds__(kHeadDim) bfd_merge_k(const float* __restrict_
 // kernels/argmax.cuh:7-72 per row (the reference's winner among ties, via argmax_key).
 __global__ void __launch_bounds__(1024) argmax_rows_k(int* __restrict__ out, const half* __restrict__ logits, int V) {
     __shared__ unsigned long long wk[32];
+    pdl_wait();
+    pdl_launch_dependents();
     const int ipt = (V + 511) / 512;
     const uint16_t* lg = reinterpret_cast<const uint16_t*>(logits + (size_t)blockIdx.x * V);
     unsigned long long best = 0;
@@ -619,6 +632,8 @@ __global__ void __launch_bounds__(1024) argmax_rows_k(int* __restrict__ out, con
 // tok = next, pos += 1, and the step's tokens appended to the output history.
 __global__ void advance_k(int* tok, int* pos, const int* next, int* hist, int* step, int B) {
     const int b = threadIdx.x;
+    pdl_wait();
+    pdl_launch_dependents();
     const int s = *step;
     if (b < B) {
         hist[(size_t)s * B + b] = next[b];
@@ -685,6 +700,7 @@ struct llmdiy_batch {
     int* ctr = nullptr;  // [num_layers] attention work counters
     bool wrows = false;  // weight-row GEMMs (env LLMDIY_BATCH_WROWS=1) instead of split-K + reduce
     int wr_fit[kWrMaxSplit + 1] = {};  // clusters of each size the weight-row GEMM fits at once
+    bool pdl = true;  // step kernels launched with programmatic dependent launch (env LLMDIY_BATCH_PDL=0: off)
     int hist_steps = 0;
     half* pf = nullptr;  // prefill scratch (kPrefillChunk rows)
     std::vector<CUtensorMap> kmaps, vmaps;  // per layer, over [max_batch * max_len][H]
@@ -703,6 +719,29 @@ int bfail(llmdiy_batch* b, int code, const std::string& m) {
     do {                                                                         \
         cudaError_t _e = (call);                                                 \
         if (_e != cudaSuccess) return bfail(b, (int)_e, std::string(what) + ": " + cudaGetErrorString(_e)); \
+    } while (0)
+
+// Launch of one step kernel; with pdl, programmatic stream serialization lets it start while the
+// previous kernel still runs (every step kernel calls pdl_wait() before touching dependent memory).
+template <class... P, class... Args>
+cudaError_t launch_step(bool pdl, void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                        Args... args) {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&lc, kern, args...);
+}
+#define BCK0(call)                                      \
+    do {                                                \
+        cudaError_t _e = (call);                        \
+        if (_e != cudaSuccess) return (int)_e;          \
     } while (0)
 
 // Split-K slices so that tiles x slices covers the SMs (every slice non-empty).
@@ -751,13 +790,15 @@ int gemm_wrows(llmdiy_batch* b, const half* A, int lda, const half* W, int N, in
     lc.blockDim = dim3(kWrThreads);
     lc.dynamicSmemBytes = sizeof(WrSmem);
     lc.stream = st;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = (unsigned)z;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     lc.attrs = at;
-    lc.numAttrs = 1;
+    lc.numAttrs = b->pdl ? 2 : 1;
     return (int)cudaLaunchKernelEx(&lc, kern, tw, tx, M, N, K, epi, err);
 }
 
@@ -793,13 +834,13 @@ int gemm_rows(llmdiy_batch* b, const half* A, int lda, const half* W, int N, int
               cudaStream_t st) {
     if (b->wrows) return gemm_wrows(b, A, lda, W, N, K, M, epi, st);
     const int z = ksplit_for(N, K, b->v.num_sms);
-    if (z == 1) return launch_gemm_tc(A, lda, W, K, M, N, K, epi, st);
+    if (z == 1) return launch_gemm_tc(A, lda, W, K, M, N, K, epi, st, 1, b->pdl);
     if ((size_t)z * M * N > b->ws_floats) return (int)cudaErrorInvalidValue;
-    int rc = launch_gemm_tc(A, lda, W, K, M, N, K, EpiPartial{b->ws, M, N}, st, z);
+    int rc = launch_gemm_tc(A, lda, W, K, M, N, K, EpiPartial{b->ws, M, N}, st, z, b->pdl);
     if (rc) return rc;
     const int threads = 4 * M * (N / 16);
-    splitk_reduce_k<<<(threads + 255) / 256, 256, 0, st>>>(b->ws, z, M, N, epi);
-    return (int)cudaGetLastError();
+    return (int)launch_step(b->pdl, splitk_reduce_k<Epi>, dim3((threads + 255) / 256), dim3(256), 0, st, b->ws, z, M,
+                            N, epi);
 }
 
 // One greedy step for sequences 0..B-1 (tok, pos on the device), enqueued on st.
@@ -809,31 +850,34 @@ int enqueue_step(llmdiy_batch* b, int B, cudaStream_t st) {
     // the attention's per-layer item counters start from zero every step
     cudaError_t ce = cudaMemsetAsync(b->ctr, 0, sizeof(int) * NL, st);
     if (ce != cudaSuccess) return (int)ce;
-    embed_rows_k<<<B, 256, 0, st>>>(v.wte, b->tok, b->x);
+    embed_rows_k<<<B, 256, 0, st>>>(v.wte, b->tok, b->x);  // after the memset: stream order
     for (int l = 0; l < NL; ++l) {
         const LayerPtrs& L = v.layers[l];
         half* kcl = b->kc + (size_t)l * b->layer_stride;
         half* vcl = b->vc + (size_t)l * b->layer_stride;
-        rmsnorm_rows_k<<<B, 256, 0, st>>>(b->xn, b->x, L.ln1);
+        BCK0(launch_step(b->pdl, rmsnorm_rows_k, dim3(B), dim3(256), 0, st, b->xn, (const half*)b->x, L.ln1));
         int rc = gemm_rows(b, b->xn, kHidden, L.qkv_w, 3 * kHidden, kHidden, B,
                            EpiQKVRows{L.qkv_b, b->q, kcl, vcl, b->pos, b->max_len}, st);
         if (rc) return rc;
-        bfd_partials_k<<<v.num_sms, 128, sizeof(BFdSmem), st>>>(b->kmaps[l], b->vmaps[l], b->q, b->pos, B,
-                                                                 b->max_len, b->Smax, b->fdp, b->ctr + l, b->err);
-        bfd_merge_k<<<B * kHeads, kHeadDim, 0, st>>>(b->fdp, b->pos, b->Smax, b->att);
+        BCK0(launch_step(b->pdl, bfd_partials_k, dim3(v.num_sms), dim3(128), sizeof(BFdSmem), st, b->kmaps[l],
+                         b->vmaps[l], (const half*)b->q, (const int*)b->pos, B, b->max_len, b->Smax, b->fdp,
+                         b->ctr + l, b->err));
+        BCK0(launch_step(b->pdl, bfd_merge_k, dim3(B * kHeads), dim3(kHeadDim), 0, st, (const float*)b->fdp,
+                         (const int*)b->pos, b->Smax, b->att));
         rc = gemm_rows(b, b->att, kHidden, L.proj_w, kHidden, kHidden, B, EpiResidual{b->x}, st);
         if (rc) return rc;
-        rmsnorm_rows_k<<<B, 256, 0, st>>>(b->xn, b->x, L.ln2);
+        BCK0(launch_step(b->pdl, rmsnorm_rows_k, dim3(B), dim3(256), 0, st, b->xn, (const half*)b->x, L.ln2));
         rc = gemm_rows(b, b->xn, kHidden, L.w12, 2 * IM, kHidden, B, EpiSwiGLU{b->act, IM}, st);
         if (rc) return rc;
         rc = gemm_rows(b, b->act, IM, L.cproj, kHidden, IM, B, EpiResidual{b->x}, st);
         if (rc) return rc;
     }
-    rmsnorm_rows_k<<<B, 256, 0, st>>>(b->xn, b->x, v.lnf);
+    BCK0(launch_step(b->pdl, rmsnorm_rows_k, dim3(B), dim3(256), 0, st, b->xn, (const half*)b->x, v.lnf));
     int rc = gemm_rows(b, b->xn, kHidden, v.lm_head, V, kHidden, B, EpiStoreRows{b->logits, V}, st);
     if (rc) return rc;
-    argmax_rows_k<<<B, 1024, 0, st>>>(b->next, b->logits, V);
-    advance_k<<<1, kBatchMax, 0, st>>>(b->tok, b->pos, b->next, b->hist, b->step, B);
+    BCK0(launch_step(b->pdl, argmax_rows_k, dim3(B), dim3(1024), 0, st, b->next, (const half*)b->logits, V));
+    BCK0(launch_step(b->pdl, advance_k, dim3(1), dim3(kBatchMax), 0, st, b->tok, b->pos, (const int*)b->next, b->hist,
+                     b->step, B));
     return (int)cudaGetLastError();
 }
 
@@ -856,6 +900,7 @@ int llmdiy_batch_create(llmdiy_engine* e, int max_batch, int max_len, llmdiy_bat
     b->Bmax = max_batch;
     b->max_len = max_len;
     if (const char* wr = std::getenv("LLMDIY_BATCH_WROWS")) b->wrows = wr[0] == '1';
+    if (const char* pd = std::getenv("LLMDIY_BATCH_PDL")) b->pdl = pd[0] != '0';
     b->Smax = (max_len + kBSplitRows - 1) / kBSplitRows;
     const size_t H = kHidden, IM = c.intermediate_size, V = c.vocab_size, NL = c.num_layers;
     b->layer_stride = (size_t)max_batch * max_len * H;

@@ -100,6 +100,23 @@ LLMDIY_DEV void tma_load_2d_hint(void* smem_dst, const void* tmap, int32_t x, in
         ::"r"(smem_u32(smem_dst)), "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// L2 prefetch of one box of a 2-D tensor map (no shared memory, no completion); x follows the
+// same 16-byte rule as the tiled loads.
+LLMDIY_DEV void tma_prefetch_2d(const void* tmap, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y)
+                 : "memory");
+}
+
+// ---------------- programmatic dependent launch ----------------
+// A kernel launched with programmatic stream serialization may start while its predecessor in the
+// stream still runs.  pdl_wait() returns once the predecessor has completed and its memory is
+// visible: a kernel calls it before its first access to memory that earlier kernels write (or
+// read, for its own writes), so the chain keeps stream order as long as every kernel in it does.
+// pdl_launch_dependents() lets the successor start its own independent prologue.  Both are
+// no-ops in a kernel launched without the attribute.
+LLMDIY_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+LLMDIY_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Bulk prefetch of a global range into L2 (no shared memory, no completion).
 LLMDIY_DEV void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes) : "memory");

@@ -23,6 +23,7 @@ constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // 128 bytes of fp16: one swizzle row
 constexpr int kGemmStages = 4;
 constexpr int kGemmThreads = 128;
+constexpr int kGemmPrefetchBlocks = 8;  // weight K blocks per CTA prefetched into L2 before pdl_wait
 
 template <int BN>
 struct GemmSmem {
@@ -64,6 +65,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_init(&s.accum, 1);
         s.fail = 0;
         mbar_fence_init();
+        // the first weight blocks into L2 while an earlier kernel may still run (weights are
+        // constant, so this needs no ordering); the loads below then find them there
+        for (int kb = 0; kb < KB && kb < kGemmPrefetchBlocks; ++kb) {
+            if constexpr (kBMN) {
+#pragma unroll
+                for (int j = 0; j < BN / 64; ++j) tma_prefetch_2d(&tmb, n0 + 64 * j, (kb0 + kb) * kGemmBK);
+            } else {
+                tma_prefetch_2d(&tmb, (kb0 + kb) * kGemmBK, n0);
+            }
+        }
     }
     if (warp == 0) {
         tmem_alloc(&s.tmem_base, kCols);
@@ -73,6 +84,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
+    pdl_wait();  // A and the epilogue's outputs depend on earlier kernels
+    pdl_launch_dependents();
 
     int issued = 0;  // producer: K blocks whose loads were issued
     if (warp == 0 && lane == 0) {

@@ -53,9 +53,11 @@ int launch_gemm_tc2(const half* A, int lda, const half* W, int ldw, int M, int N
     return (int)cudaGetLastError();
 }
 
+// pdl: launch with programmatic stream serialization (the kernel prefetches its first weight
+// blocks into L2, then waits for the previous kernel before reading A or running the epilogue).
 template <class Epi>
 int launch_gemm_tc(const half* A, int lda, const half* W, int ldw, int M, int N, int K, const Epi& epi,
-                   cudaStream_t st, int ksplit = 1) {
+                   cudaStream_t st, int ksplit = 1, bool pdl = false) {
     if (M <= 0 || N <= 0 || K <= 0) return (int)cudaErrorInvalidValue;
     // SM pairs when there are at least as many 256 x 256 tiles as pairs (below that, 128 x 256
     // tiles on single SMs cover more of the GPU)
@@ -77,8 +79,21 @@ int launch_gemm_tc(const half* A, int lda, const half* W, int ldw, int M, int N,
     const int per = (KB + ksplit - 1) / ksplit;
     if ((ksplit - 1) * per >= KB) return (int)cudaErrorInvalidValue;  // an empty slice
     dim3 grid((N + BN - 1) / BN, (M + kGemmBM - 1) / kGemmBM, ksplit);
-    kern<<<grid, kGemmThreads, sizeof(GemmSmem<BN>), st>>>(ta, tb, M, N, K, epi, err);
-    return (int)cudaGetLastError();
+    if (!pdl) {
+        kern<<<grid, kGemmThreads, sizeof(GemmSmem<BN>), st>>>(ta, tb, M, N, K, epi, err);
+        return (int)cudaGetLastError();
+    }
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = dim3(kGemmThreads);
+    lc.dynamicSmemBytes = sizeof(GemmSmem<BN>);
+    lc.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&lc, kern, ta, tb, M, N, K, epi, err);
 }
 
 // C = A[M,K] * B[K,N] with B in the reference's [K,N] layout (MN-major operand).

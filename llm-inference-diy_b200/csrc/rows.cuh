@@ -11,6 +11,8 @@ namespace llmdiy {
 static __global__ void __launch_bounds__(256) embed_rows_k(const half* __restrict__ wte, const int* __restrict__ tokens,
                                                     half* __restrict__ x) {
     const int r = blockIdx.x, t = threadIdx.x;
+    pdl_wait();
+    pdl_launch_dependents();
     const half* src = wte + (size_t)tokens[r] * kHidden;
     *reinterpret_cast<uint4*>(x + (size_t)r * kHidden + 8 * t) = *reinterpret_cast<const uint4*>(src + 8 * t);
 }
@@ -20,8 +22,10 @@ static __global__ void __launch_bounds__(256) rmsnorm_rows_k(half* __restrict__ 
                                                       const half* __restrict__ w) {
     __shared__ float red[17];
     const int r = blockIdx.x, t = threadIdx.x;
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * t);  // weights: no dependence on earlier kernels
+    pdl_wait();
+    pdl_launch_dependents();
     const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)r * kHidden + 8 * t);  // this thread's 8 values
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * t);
     const float s = rms_scale_regs2048(v, 1e-6f, red, t, 1);
     float xf[8], wf[8], of[8];
     unpack8(v, xf);
