@@ -66,8 +66,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         s.fail = 0;
         mbar_fence_init();
         // the first weight blocks into L2 while an earlier kernel may still run (weights are
-        // constant, so this needs no ordering); the loads below then find them there
-        for (int kb = 0; kb < KB && kb < kGemmPrefetchBlocks; ++kb) {
+        // constant, so this needs no ordering); the loads below then find them there.  Only with
+        // one M tile: with more, every M tile's CTA would prefetch the same weight blocks
+        for (int kb = 0; gridDim.y == 1 && kb < KB && kb < kGemmPrefetchBlocks; ++kb) {
             if constexpr (kBMN) {
 #pragma unroll
                 for (int j = 0; j < BN / 64; ++j) tma_prefetch_2d(&tmb, n0 + 64 * j, (kb0 + kb) * kGemmBK);
