@@ -615,7 +615,7 @@ __device__ __forceinline__ void kv_rows_fold(const uint4* kr, const uint4* vr, i
 }
 
 // Split-KV attention of one (head, split) per CTA (qwen_infer.cu:646-677 with
-// the reference's flash-decoding split, kernels/flash_decoding.cuh): the
+// the reference's split-KV flash decoding, kernels/flash_decode_q1_opt.cuh:548-724): the
 // CTA's rows < pos come from the KV cache, the query and row pos from the
 // QKV phase's words.  Each warp folds its cached rows eight at a time (one
 // L2 round trip per eight rows).  Splits 1..8 publish (o, m, l) partials as

@@ -22,7 +22,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_LIB = os.path.join(HERE, "_build", "libqwen_oracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libref_kernels.so")
 REF_ENGINE = os.path.join(HERE, "_ref", "qwen_infer_ref")
-REFERENCE_TREE = "/root/reference"
+# The reference checkout: $LLMDIY_REFERENCE_TREE, else a `reference` directory beside this repository.
+REFERENCE_TREE = os.environ.get("LLMDIY_REFERENCE_TREE",
+                                os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 
 def build(reference: bool = True) -> None:
@@ -74,6 +76,7 @@ class Oracle:
             "orc_model_prefill": ([P, P, I], None),
             "orc_model_generate": ([P, P, I, I, I, P], I),
             "orc_model_kcache": ([P, I], P),
+            "orc_write_random_bin": ([ctypes.c_char_p, ctypes.POINTER(OrcConfig), ctypes.c_uint64, F, I], I),
             "orc_model_vcache": ([P, I], P),
         }
         for name, (args, res) in sig.items():
@@ -155,6 +158,14 @@ class Oracle:
         O = np.zeros(128, np.float16)
         self.L.orc_fd_stage2(_ptr(Op), _ptr(lse), _ptr(O), lse.size)
         return O
+
+    def write_random_bin(self, path, vocab_size, hidden_size, num_layers, num_heads, intermediate_size,
+                         max_seqlen, seed, std_dev=0.02, nthreads=8):
+        """Seeded random QWDF file (the benchmark's synthetic model), without the product library."""
+        c = OrcConfig(0x46445751, vocab_size, hidden_size, num_layers, num_heads, intermediate_size, max_seqlen)
+        rc = self.L.orc_write_random_bin(path.encode(), ctypes.byref(c), seed, std_dev, nthreads)
+        if rc != 0:
+            raise OSError(f"could not write {path}")
 
     def causal_attention(self, Q, K, V, N, stride_q, stride_kv, hd=128, nthreads=8):
         Q, K, V = f16(Q), f16(K), f16(V)

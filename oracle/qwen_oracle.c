@@ -686,3 +686,76 @@ int orc_model_generate(orc_model* m, const int* prompt, int n, int max_new, int 
     }
     return cnt;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Seeded random QWDF file: the synthetic weights of the benchmark configs.  */
+/* The reference has no such writer; this restates the generator of the     */
+/* library under test (per tensor id a splitmix64 key, Box-Muller pairs in   */
+/* double, then double -> float -> fp16 RNE; norm weights 1.0), so the       */
+/* reference arm of the bench and the tests produce the same bytes without   */
+/* loading that library.  Layout: model_weights/convert_weights.py:107-185.   */
+/* ------------------------------------------------------------------------ */
+static uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+typedef struct { uint64_t key; double sd; uint64_t first; f16* out; } rnd_ctx;
+
+/* elements [first + b, first + e) of a tensor; pair p holds elements 2p (cos) and 2p+1 (sin) */
+static void rnd_range(void* c, int64_t b, int64_t e) {
+    rnd_ctx* g = (rnd_ctx*)c;
+    for (int64_t i = b; i < e; i++) {
+        const uint64_t gi = g->first + (uint64_t)i, p = gi / 2;
+        const uint64_t u = splitmix64(g->key + 2 * p), v = splitmix64(g->key + 2 * p + 1);
+        const double u1 = (double)((u >> 11) + 1) * (1.0 / 9007199254740992.0);
+        const double u2 = (double)(v >> 11) * (1.0 / 9007199254740992.0);
+        const double r = sqrt(-2.0 * log(u1)), a = 6.283185307179586476925286766559 * u2;
+        const double z = (gi & 1) ? r * sin(a) : r * cos(a);
+        g->out[i] = f2h((float)(z * g->sd));
+    }
+}
+
+int orc_write_random_bin(const char* path, const orc_config* cfg, uint64_t seed, float std_dev, int nthreads) {
+    FILE* f = fopen(path, "wb");
+    if (!f) return -1;
+    orc_config h = *cfg;
+    h.magic = 0x46445751u;
+    int ok = fwrite(&h, sizeof(h), 1, f) == 1;
+    const uint64_t H = h.hidden_size, IM = h.intermediate_size, V = h.vocab_size;
+    const int NL = (int)h.num_layers, nt = 1 + 8 * NL + 2;
+    const size_t chunk = (size_t)1 << 24;
+    f16* buf = (f16*)malloc(sizeof(f16) * chunk);
+    pool_t* pool = pool_new(nthreads);
+    for (int id = 0; ok && id < nt; id++) {
+        uint64_t n;
+        int norm = 0;
+        if (id == 0 || id == nt - 1) n = V * H;
+        else if (id == nt - 2) { n = H; norm = 1; }
+        else switch ((id - 1) % 8) {
+            case 0: case 4: n = H; norm = 1; break;          /* ln_1, ln_2 */
+            case 1: n = 3 * H * H; break;                    /* qkv_w */
+            case 2: n = 3 * H; break;                        /* qkv_b */
+            case 3: n = H * H; break;                        /* attn_proj_w */
+            case 5: case 6: n = IM * H; break;               /* ffn_w1, ffn_w2 */
+            default: n = H * IM; break;                      /* ffn_proj_w */
+        }
+        const uint64_t key = splitmix64(seed ^ (0xD1B54A32D192ED03ull * (uint64_t)(id + 1)));
+        for (uint64_t i = 0; ok && i < n; i += chunk) {
+            const size_t m = (size_t)(n - i < chunk ? n - i : chunk);
+            if (norm) {
+                for (size_t k = 0; k < m; k++) buf[k] = f2h(1.0f);
+            } else {
+                rnd_ctx rc = {key, (double)std_dev, i, buf};
+                par_for(pool, (int64_t)m, 1 << 16, rnd_range, &rc);
+            }
+            ok = fwrite(buf, sizeof(f16), m, f) == m;
+        }
+    }
+    pool_free(pool);
+    free(buf);
+    ok = (fclose(f) == 0) && ok;
+    return ok ? 0 : -1;
+}

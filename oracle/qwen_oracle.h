@@ -95,6 +95,11 @@ void orc_model_prefill(orc_model* m, const int* tokens, int n);
  * then up to max_new greedy steps.  stop_on_eos: stop at 151643/151645.
  * Returns the number of tokens written to out. */
 int  orc_model_generate(orc_model* m, const int* prompt, int n, int max_new, int stop_on_eos, int* out);
+/* Writes a QWDF file of seeded N(0, std_dev) fp16 weights (norm weights 1) with the
+ * header *cfg (magic filled in): the synthetic model of the benchmark configs, byte for
+ * byte the one the library under test generates for the same (cfg, seed, std_dev).
+ * Returns 0, or -1 on an I/O error. */
+int  orc_write_random_bin(const char* path, const orc_config* cfg, uint64_t seed, float std_dev, int nthreads);
 /* read-only views used by tests */
 const orc_f16* orc_model_kcache(const orc_model* m, int layer);
 const orc_f16* orc_model_vcache(const orc_model* m, int layer);

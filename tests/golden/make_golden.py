@@ -3,7 +3,7 @@ kernels and engine (LLM-inference-DIY), compiled from their sources by
 `make -C oracle ref` into oracle/_ref as compute_89 PTX and JIT-run on a B200.
 
 Run on a GPU box from the repository root:
-    python tests/golden/make_golden.py [outdir] [--engine]
+    python tests/golden/make_golden.py OUTPUT_DIR [--engine]
 It writes ref_ops.npz (seeded inputs and the reference kernels' outputs) and
 ref_engine.json (token streams of the reference engine qwen_infer on a
 seeded random-weight QWDF file).  Inputs are regenerated from the stored
@@ -147,4 +147,6 @@ def main(outdir, engine=False):
 
 if __name__ == "__main__":
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
-    main(args[0] if args else os.path.join(ROOT, "gpurun_out", "golden"), engine="--engine" in sys.argv)
+    if len(args) != 1:
+        sys.exit("usage: make_golden.py OUTPUT_DIR [--engine]")
+    main(args[0], engine="--engine" in sys.argv)

@@ -151,3 +151,19 @@ def test_engine_create_fails_cleanly_without_valid_config():
     cfg = L.make_config(hidden_size=1024, num_heads=8)  # not the 2048/16x128 the fused kernel is built for
     with pytest.raises(L.LlmdiyError):
         L.Engine(config=cfg)
+
+
+def test_oracle_random_writer_matches_library():
+    """The oracle's seeded writer (used where the product library must not be loaded: the bench's
+    reference arm) produces the library's file byte for byte, here with two layers and a ragged
+    intermediate size."""
+    import oracle as orc
+    cfg = L.make_config(vocab_size=300, hidden_size=2048, num_layers=2, num_heads=16, intermediate_size=96,
+                        max_seqlen=32)
+    d = tempfile.mkdtemp()
+    p1, p2 = os.path.join(d, "lib.bin"), os.path.join(d, "orc.bin")
+    L.write_random_bin(p1, cfg, seed=1234, nthreads=4)
+    orc.Oracle().write_random_bin(p2, **cfg.as_dict(), seed=1234, nthreads=3)
+    assert open(p1, "rb").read() == open(p2, "rb").read()
+    os.remove(p1)
+    os.remove(p2)
