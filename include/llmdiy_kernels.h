@@ -87,8 +87,10 @@ int llmdiy_fd_mh_status(const float* work, int L, int num_heads);
 
 /* Multi-GPU exchange of the shards' partials over peer memory (no counterpart in the reference,
  * which has no multi-GPU path; replaces an all-gather + llmdiy_fd_mh_merge).  Every rank owns a
- * receive buffer of llmdiy_p2p_buffer_bytes(world, num_heads) bytes ([world][num_heads][130] fp32
- * partials, then [world][num_heads] u32 flags), allocated with llmdiy_p2p_alloc, whose CUDA IPC
+ * receive buffer of llmdiy_p2p_buffer_bytes(world, num_heads) bytes (two regions, used by calls of odd
+ * and even tag, each [world][num_heads][130] fp32 partials then [world][num_heads] u32 flags, so a rank
+ * may start the next call while a slower rank still merges the last one), allocated with
+ * llmdiy_p2p_alloc, whose CUDA IPC
  * handle (64 bytes) the other ranks open with llmdiy_p2p_open.  llmdiy_fd_p2p_merge, called by every
  * rank with the same tag (a call counter starting at 1), stores this rank's [num_heads][130] partial
  * into slot `rank` of every rank's buffer (peers[] = device array of the world buffer pointers in rank
@@ -108,8 +110,10 @@ int llmdiy_fd_p2p_merge(const float* part, const uint64_t* peers, int world, int
  * with num_chunks = ceil(L/256), but the chunk partials live in a file-scope device array (33,536 bytes)
  * instead of caller buffers.  L may be at most 32768 rows (128 chunks); a larger L returns -1 before
  * anything is launched.  The first call on each device looks the array up with cudaGetSymbolAddress and
- * should come before any stream capture.  Every call on a device shares the array: calls whose work
- * overlaps on the GPU race; calls ordered on one stream do not. */
+ * should come before any stream capture; so should the first call after a cudaDeviceReset (the address
+ * is cached per device and CUDA context, and looked up again when the context changes).  Every call
+ * on a device shares the array: calls whose work overlaps on the GPU race; calls ordered on one stream
+ * do not. */
 int llmdiy_fd_split_noalloc(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int L, int stride,
                             void* stream);
 

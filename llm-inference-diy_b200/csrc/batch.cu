@@ -82,7 +82,7 @@ struct EpiQKVRows {
         if (sec == 2) {
             *reinterpret_cast<uint4*>(vc + crow + o1) = pack8(y1);
             *reinterpret_cast<uint4*>(vc + crow + o1 + 64) = pack8(y2);
-            return;
+            return;  // an epilogue: its kernel has passed pdl_wait() before any epilogue runs
         }
         float r1[8], r2[8];
 #pragma unroll
@@ -457,7 +457,7 @@ __global__ void __launch_bounds__(128, 1)
     pc.tile = pc.ntiles = 0;
     bool pdone = false;
     uint32_t nclaimed = 0, issued = 0, consumed = 0;
-    auto produce = [&]() {
+    auto produce = [&]() {  // runs after the kernel's pdl_wait(); its returns end a claim, not the CTA
         if (pdone) return;
         bool first = false;
         while (pc.tile >= pc.ntiles) {

@@ -299,7 +299,16 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_merge_ranks_k(const float* __re
 // Exchange + merge over peer memory (one CTA per head): push this rank's partial of head h into
 // slot `rank` of every rank's buffer, publish a flag per (rank, head) after a system-scope fence,
 // wait for every rank's flag in the own buffer, then merge the world's partials in rank order.
+//
+// Each buffer holds two regions, [2] x {partials [world][H][130] fp32, flags [world][H] u32}, and
+// call `tag` uses region (tag & 1).  A rank that has finished call t saw every rank's call-t flags,
+// and a rank raises those only after its own call t-1 kernel (same stream) has finished merging; so
+// the earliest next write into a region, call t+1's, lands after every reader of call t-1 in that
+// region is done, while call t's region may still be read.  One region would let a fast rank's
+// call t+1 overwrite a slot that a slower rank's call t merge is still reading.
 constexpr uint32_t kP2pPollLimit = 1u << 20;  // about a second of polling
+
+__host__ __device__ inline size_t p2p_region_floats(int world, int H) { return (size_t)world * H * (kFdPart + 1); }
 
 __global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __restrict__ part,
                                                              const unsigned long long* __restrict__ peers, int world,
@@ -308,10 +317,11 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __rest
     __shared__ float scratch[8 * kFdPart];
     __shared__ float red[4];
     const int h = blockIdx.x, d = threadIdx.x;
-    const size_t flag_off = (size_t)world * H * kFdPart;  // floats before the flags
+    const size_t region = (tag & 1u) * p2p_region_floats(world, H);  // floats before this call's region
+    const size_t flag_off = region + (size_t)world * H * kFdPart;   // floats before its flags
     const float* src = part + (size_t)h * kFdPart;
     for (int p = 0; p < world; ++p) {
-        float* dst = reinterpret_cast<float*>(peers[p]) + ((size_t)rank * H + h) * kFdPart;
+        float* dst = reinterpret_cast<float*>(peers[p]) + region + ((size_t)rank * H + h) * kFdPart;
         for (int i = d; i < kFdPart; i += kFdHeadDim) dst[i] = src[i];
     }
     __syncthreads();  // every thread's stores are issued before thread 0's fence
@@ -338,7 +348,7 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __rest
         if (d == 0) atomicExch(err, 1);
         return;
     }
-    fd_merge_head(own + (size_t)h * kFdPart, world, H * kFdPart, scratch, 8 * kFdPart, red,
+    fd_merge_head(own + region + (size_t)h * kFdPart, world, H * kFdPart, scratch, 8 * kFdPart, red,
                   O + (size_t)h * kFdHeadDim, nullptr);
 }
 
@@ -479,7 +489,7 @@ extern "C" int llmdiy_fd_mh_status(const float* work, int L, int num_heads) {
 
 extern "C" size_t llmdiy_p2p_buffer_bytes(int world, int num_heads) {
     if (world <= 0 || num_heads <= 0) return 0;
-    const size_t b = (size_t)world * num_heads * (kFdPart * sizeof(float) + sizeof(uint32_t));
+    const size_t b = 2 * p2p_region_floats(world, num_heads) * sizeof(float);  // two regions (tag parity)
     return (b + 255) / 256 * 256;
 }
 

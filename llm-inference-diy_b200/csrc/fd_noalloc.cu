@@ -13,6 +13,8 @@
 // the partials need no clearing (each chunk writes its own before the merge
 // reads it).  Two calls whose work overlaps on the GPU (different streams,
 // no ordering between them) race on the array and give undefined results.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "ops.cuh"
@@ -32,7 +34,8 @@ static __device__ __align__(256) unsigned char g_fd_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_ptr_mu;
-void* g_ptr[kMaxDevices];  // cudaGetSymbolAddress(g_fd_scratch) per device, filled on first use
+void* g_ptr[kMaxDevices];                // cudaGetSymbolAddress(g_fd_scratch) per device
+unsigned long long g_ctx_id[kMaxDevices];  // the context that address belongs to (0 = none yet)
 
 __global__ void __launch_bounds__(256) fd_split_noalloc_k(const half* __restrict__ Q, const half* __restrict__ K,
                                                          const half* __restrict__ V, half* __restrict__ O, int L,
@@ -107,19 +110,47 @@ __global__ void __launch_bounds__(256) fd_split_noalloc_k(const half* __restrict
     }
 }
 
-// Device address of g_fd_scratch for the current device, looked up once per
-// device.  The first call on a device must not be inside a stream capture.
+// The unique id of the calling thread's current CUDA context (cuCtxGetCurrent + cuCtxGetId,
+// through the runtime's driver entry points), or 0 when there is none or the driver lacks them.
+unsigned long long current_ctx_id() {
+    using GetCurrent = CUresult (*)(CUcontext*);
+    using GetId = CUresult (*)(CUcontext, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
+
+// Device address of g_fd_scratch for the current device, looked up once per device and context:
+// the first call on a device (and the first after cudaDeviceReset, whose new context gets a new id)
+// does the lookup and must not be inside a stream capture; later calls reuse the address.
 int scratch_ptr(unsigned char** out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
     if (dev < 0 || dev >= kMaxDevices) return (int)cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(g_ptr_mu);
-    if (!g_ptr[dev]) {
+    const unsigned long long id = current_ctx_id();
+    if (!g_ptr[dev] || id == 0 || id != g_ctx_id[dev]) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_fd_scratch);
         if (e != cudaSuccess) return (int)e;
         g_ptr[dev] = p;
+        g_ctx_id[dev] = current_ctx_id();  // the lookup made the device's context current if it was not
     }
     *out = static_cast<unsigned char*>(g_ptr[dev]);
     return 0;

@@ -259,6 +259,7 @@ class RefKernels:
             "ref_gather_kv_from_cache": [P, P, I, I],
             "ref_scatter_interleaved": [P, P, I, I, I],
             "ref_transpose": [P, P, I, I],
+            "ref_fd_layer": [P, P, P, P, P, P, I, I, I, P],
         }
         for name, args in sig.items():
             fn = getattr(L, name)

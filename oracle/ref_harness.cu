@@ -80,6 +80,26 @@ int ref_fd_opt_stage2(const half* Opart, const float* LSE, half* O, int num_chun
     return (int)cudaDeviceSynchronize();
 }
 
+// The decode step's whole attention launch sequence for one layer (qwen_infer.cu:646-677): per
+// head, the fused kernel when L <= 256, else split stage 1 over ceil(L/256) chunks and stage 2,
+// with the partials buffer reused head after head.  Launched on `stream` without synchronising
+// (for timing, also inside a CUDA graph); q/out are [nh*128], K/V the cache rows at `stride`.
+int ref_fd_layer(const half* q, const half* Kc, const half* Vc, half* out, half* Opart, float* LSE, int L, int nh,
+                 int stride, cudaStream_t stream) {
+    const int num_chunks = (L + 255) / 256;
+    for (int h = 0; h < nh; h++) {
+        if (num_chunks == 1) {
+            fd_v5_fused_kernel<128, 8, 32><<<1, 256, 0, stream>>>(q + h * 128, Kc + h * 128, Vc + h * 128,
+                                                                  out + h * 128, L, stride);
+        } else {
+            fd_v5_split_stage1_kernel<128, 256, 8><<<num_chunks, 256, 0, stream>>>(
+                q + h * 128, Kc + h * 128, Vc + h * 128, Opart, LSE, L, num_chunks, stride);
+            fd_opt_stage2_kernel<128><<<1, 128, 0, stream>>>(Opart, LSE, out + h * 128, num_chunks);
+        }
+    }
+    return (int)cudaGetLastError();
+}
+
 // qwen_infer.cu:731
 int ref_argmax(int* out, const half* logits, int V) {
     argmax_kernel<<<1, 512>>>(out, logits, V);

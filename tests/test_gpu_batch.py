@@ -126,3 +126,25 @@ def test_batch_weight_row_gemms_match_splitk_at_64(engine, monkeypatch):
         if t0[-1, s] != t1[-1, s]:
             top = np.sort(l1[s])[-2:]
             assert top[1] - top[0] < 2e-2, s
+
+
+def test_batch_overlapped_launch_matches_serial(engine, monkeypatch):
+    """The batched step with programmatic dependent launch (the default: every step kernel may
+    start before the previous one ends and waits on it in every CTA) against plain serial
+    launches (LLMDIY_BATCH_PDL=0) on the same caches and tokens: identical tokens and logits
+    bit for bit, over several steps at a ragged batch."""
+    rng = np.random.default_rng(53)
+    B, steps = 24, 6
+    lens = rng.integers(1, 900, B).tolist()
+    toks = rng.integers(0, SMALL["vocab_size"], B).tolist()
+    out = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("LLMDIY_BATCH_PDL", mode)
+        b = L.Batch(engine, max_batch=B, max_len=920)
+        for s in range(B):
+            b.fill_random(s, lens[s], seed=900 + s)
+        t = b.decode(toks, lens, steps)
+        out[mode] = (t, np.stack([b.logits(s).view(np.uint16) for s in range(B)]))
+        b.close()
+    assert np.array_equal(out["0"][0], out["1"][0])
+    assert np.array_equal(out["0"][1], out["1"][1])

@@ -41,11 +41,6 @@ def omodel(small_bin):
     return orc.OracleModel(small_bin, nthreads=os.cpu_count() or 8)
 
 
-def top2_margin(logits):
-    v = np.sort(logits.astype(np.float32))
-    return float(v[-1] - v[-2])
-
-
 def test_random_engine_equals_file_engine(small_bin, engine):
     e2 = L.Engine(config=L.make_config(**SMALL), seed=SEED)
     engine.reset()
@@ -59,19 +54,25 @@ def test_random_engine_equals_file_engine(small_bin, engine):
 
 
 def test_step_matches_oracle(engine, omodel):
+    """40 teacher-forced steps: both sides get the oracle's token at every step, so a near-tie
+    cannot end the check early; a differing argmax is accepted only where the oracle's logits of
+    the two candidates are at most one fp16 ulp apart."""
+    from gpu_util import f16_ulp
     engine.reset()
     omodel.reset()
-    tok = 123
+    tok, n_diff = 123, 0
     for pos in range(40):
         g = engine.step(tok, pos)
         lg = engine.logits().astype(np.float32)
         o, olg, _ = omodel.step(tok, pos, want_logits=True)
-        err = float(np.max(np.abs(lg - olg.astype(np.float32))))
+        olg = olg.astype(np.float32)
+        err = float(np.max(np.abs(lg - olg)))
         assert err < 2e-2, (pos, err)
         if g != o:
-            assert top2_margin(olg) < 4e-3, (pos, g, o, top2_margin(olg))
-            break
-        tok = g
+            n_diff += 1
+            assert olg[o] - olg[g] <= f16_ulp(olg[o]), (pos, g, o, float(olg[o] - olg[g]))
+        tok = o
+    assert n_diff <= 2, n_diff
     k, v = engine.kv(1, 0, 40)
     ok_, ov = omodel.kv(1, 0, 40)
     assert float(np.max(np.abs(k.astype(np.float32) - ok_.astype(np.float32)))) < 2e-2

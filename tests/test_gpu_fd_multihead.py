@@ -127,6 +127,14 @@ def test_fd_p2p_exchange_single_rank(oracle, rng):
     t = torch()
     H, stride, n = 16, 2048, 3000
     ex = D.P2PExchange(None, H, t.device("cuda"))
+
+    class _View:  # the exchange's own receive buffer as a float32 tensor (no copy)
+        def __init__(self, ptr, n):
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 2}
+
+    region = H * 131  # floats per region: [1][H][130] partials + [1][H] flags
+    buf = t.as_tensor(_View(ex.own, 2 * region), device="cuda")
+    parts = []
     try:
         for call in range(3):
             q, K, V = _inputs(rng, n, H, stride)
@@ -143,6 +151,13 @@ def test_fd_p2p_exchange_single_rank(oracle, rng):
             for h in (0, 7, H - 1):
                 exp = oracle.attention_q1(q[h * 128:(h + 1) * 128], K[h * 128:], V[h * 128:], n, stride)
                 assert max_abs(got[h], exp) < 1e-3, (call, h)
+            # call `tag` writes region (tag & 1); the other region keeps the previous call's partial
+            parts.append(part.clone())
+            r = (call + 1) & 1
+            assert t.equal(buf[r * region: r * region + H * 130].view(H, 130), part)
+            if call:
+                r0 = call & 1
+                assert t.equal(buf[r0 * region: r0 * region + H * 130].view(H, 130), parts[call - 1])
     finally:
         ex.close()
 

@@ -36,9 +36,10 @@ def test_fd_split_noalloc_matches_pair_twice():
     import torch
     fn = _noalloc()
     rng = np.random.default_rng(20261201)
-    # (rows, row stride in halves): a long cache, then a short ragged one, both
-    # through the same scratch array back to back on one stream
-    cases = [(9000, 2048), (333, 128)]
+    # (rows, row stride in halves), all through the same scratch array back to back on one stream:
+    # a long cache, a short ragged one, one chunk (the only CTA also merges), an exact multiple of
+    # the 256-row chunk, and the stated maximum (every scratch slot and the full merge loop)
+    cases = [(9000, 2048), (333, 128), (200, 2048), (512, 128), (MAX_ROWS, 128)]
     outs = []
     for L_, stride in cases:
         q = torch.from_numpy(rng.standard_normal(128).astype(np.float16)).cuda()
