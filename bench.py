@@ -563,11 +563,12 @@ def fd_op_leg(args, rank, world, local, pg):
         lse = torch.empty(nc, dtype=torch.float32, device=dev)
         Or = torch.empty(FD_HEADS * 128, dtype=torch.float16, device=dev)
 
+        rs = torch.cuda.Stream(device=dev)
+
         def ref():
             refk.fd_layer(q.data_ptr(), K.data_ptr(), V.data_ptr(), Or.data_ptr(), Op.data_ptr(), lse.data_ptr(),
-                          Lt, FD_HEADS, FD_STRIDE, ctypes.c_void_p(st.cuda_stream))
+                          Lt, FD_HEADS, FD_STRIDE, ctypes.c_void_p(rs.cuda_stream))
 
-        rs = torch.cuda.Stream(device=dev)
         rus = _graph_us(torch, rs, ref, max(1, args.steps), max(1, args.warmup))
         call()
         torch.cuda.synchronize()

@@ -126,13 +126,20 @@ int llmdiy_argmax(int* out, const uint16_t* logits, int V, void* stream);
 int llmdiy_hgemv(const uint16_t* A, const uint16_t* B, uint16_t* C, int N, int K, void* stream);
 
 /* kernels/hgemm_mma_swizzle.cuh:414 hgemm_swizzle_nn(A, B, C, M, N, K): row-major C[M,N] = A[M,K] * B[K,N]
- * (qwen_infer.cu:364-366).  Accumulates in fp32 (the reference accumulates in fp16). */
+ * (qwen_infer.cu:364-366).  Accumulates in fp32 (the reference accumulates in fp16).  Runs on the tcgen05
+ * tensor cores when N and K are multiples of 8 and the pointers 16-byte aligned (the row pitches a TMA
+ * descriptor can address), else on CUDA cores. */
 int llmdiy_hgemm_swizzle_nn(uint16_t* A, uint16_t* B, uint16_t* C, int M, int N, int K, void* stream);
+/* Which kernel llmdiy_hgemm_swizzle_nn runs for these arguments, without running it (host only, no CUDA
+ * call): 1 = tcgen05 tensor cores, 0 = CUDA cores, -1 = invalid shape.  No counterpart in the reference. */
+int llmdiy_hgemm_swizzle_nn_path(const uint16_t* A, const uint16_t* B, const uint16_t* C, int M, int N, int K);
 
 /* kernels/flash_attn.cu:1854 flash_attn_tuned_A_kernel<128,...>(Q, K, V, O, QKV_seqlen, QKV_head,
  * stride_Q, stride_KV, K_ofs_override, V_ofs_override, Q_ofs_override, O_ofs_override) with the causal
  * mask the engine compiles in (FLASH_ATTN_CAUSAL, qwen_infer.cu:62, launched per head at :501-516).
- * Offsets < 0 mean "derive from QKV_head" exactly as the reference does. */
+ * Offsets < 0 mean "derive from QKV_head" exactly as the reference does.  Runs the tcgen05 flash
+ * attention of the engine's prefill on the one head (P in fp16, fp32 accumulation); row pitches must be
+ * multiples of 8 elements and the rows 16-byte aligned. */
 int llmdiy_flash_attn_tuned_A(uint16_t* Q, uint16_t* K, uint16_t* V, uint16_t* O, int N, int QKV_head,
                               int stride_Q, int stride_KV, int K_ofs, int V_ofs, int Q_ofs, int O_ofs, void* stream);
 

@@ -46,6 +46,10 @@ LLMDIY_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
 LLMDIY_DEV void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// `count` arrivals at once (release semantics at CTA scope, like a plain arrive).
+LLMDIY_DEV void mbar_arrive_cnt(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
 LLMDIY_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(

@@ -332,10 +332,10 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __rest
             asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f + (size_t)rank * H + h), "r"(tag) : "memory");
         }
     }
-    float* own = reinterpret_cast<float*>(peers[rank]);
+    const float* own = reinterpret_cast<const float*>(peers[rank]) + region;  // this call's region here
     bool ok = true;
     if (d < world) {
-        const unsigned int* f = reinterpret_cast<const unsigned int*>(own + flag_off) + (size_t)d * H + h;
+        const unsigned int* f = reinterpret_cast<const unsigned int*>(own + (size_t)world * H * kFdPart) + d * H + h;
         ok = false;
         for (uint32_t i = 0; i < kP2pPollLimit; ++i) {
             unsigned int v;
@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __rest
         if (d == 0) atomicExch(err, 1);
         return;
     }
-    fd_merge_head(own + region + (size_t)h * kFdPart, world, H * kFdPart, scratch, 8 * kFdPart, red,
+    fd_merge_head(own + (size_t)h * kFdPart, world, H * kFdPart, scratch, 8 * kFdPart, red,
                   O + (size_t)h * kFdHeadDim, nullptr);
 }
 

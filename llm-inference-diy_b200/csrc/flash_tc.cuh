@@ -51,11 +51,12 @@ struct FlashTcSmem {
     int fail;
 };
 
-// tq: the chunk's query rows [n][2048] (box 64 x 128); tk, tv: one layer's K / V cache
-// [rows][2048] (box 64 x 64).  att: [n][2048].  Grid (ceil(n/128), 16 heads).
+// tq: the query rows [n][heads*128] (box 64 x 128); tk, tv: the K / V rows [rows][heads*128]
+// (box 64 x 64), head h in columns h*128 .. h*128+127 of each.  att: [n] rows of ldo elements,
+// head h at column h*128.  Grid (ceil(n/128), heads).
 __global__ void __launch_bounds__(kFtThreads, 2)
     flash_tc_k(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-               const __grid_constant__ CUtensorMap tv, half* __restrict__ att, int n, int p0, int* err) {
+               const __grid_constant__ CUtensorMap tv, half* __restrict__ att, int ldo, int n, int p0, int* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     FlashTcSmem& s = *reinterpret_cast<FlashTcSmem*>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -257,7 +258,7 @@ __global__ void __launch_bounds__(kFtThreads, 2)
             tc_fence_after();
             const bool live = q0 + r < n;
             const float inv = 1.f / l;
-            half* dst = att + (size_t)(q0 + r) * kHidden + h * kHeadDim;
+            half* dst = att + (size_t)(q0 + r) * ldo + h * kHeadDim;
 #pragma unroll 1
             for (int c = 0; c < kHeadDim; c += 16) {
                 uint32_t o[16];

@@ -100,7 +100,7 @@ int launch_gemm_tc(const half* A, int lda, const half* W, int ldw, int M, int N,
 template <class Epi>
 int launch_gemm_tc_kn(const half* A, int lda, const half* B, int ldb, int M, int N, int K, const Epi& epi,
                       cudaStream_t st) {
-    if (M <= 0 || N <= 0 || K <= 0 || (N % 64)) return (int)cudaErrorInvalidValue;
+    if (M <= 0 || N <= 0 || K <= 0 || (N % 8) || (K % 8)) return (int)cudaErrorInvalidValue;
     constexpr int BN = kGemmBN;
     CUtensorMap ta, tb;
     if (!make_kmajor_map(&ta, A, M, K, lda, kGemmBM) || !make_mnmajor_map(&tb, B, K, N, ldb))

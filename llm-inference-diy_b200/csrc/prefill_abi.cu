@@ -5,16 +5,16 @@
 // These are the op-level entry points for callers that hold row-major
 // [K,N] weights and per-head attention buffers, exactly as the reference's
 // prefill does: the GEMM runs on the tcgen05 tensor cores (B staged
-// MN-major), the attention on the flash-attention kernel of the engine's
-// prefill; both accumulate in fp32 (the reference accumulates the GEMM and
-// the attention scores in fp16).  Shapes the TMA path cannot take (N not a
-// multiple of 64, unaligned rows) use the CUDA-core kernels below.
-#include <mutex>
-
-#include "flash_prefill.cuh"
+// MN-major by TMA), the attention on the tcgen05 flash-attention kernel of
+// the engine's prefill (flash_tc.cuh) for one head; both accumulate in fp32
+// (the reference accumulates the GEMM and the attention scores in fp16).
+// A GEMM whose row pitches a TMA descriptor cannot express (N or K not a
+// multiple of 8 elements, or a pointer not 16-byte aligned) runs on the
+// CUDA-core kernel below.
 #include "gemm_tc_host.h"
 #include "llmdiy_kernels.h"
 #include "ops.cuh"
+#include "prefill_tc.h"
 
 using namespace llmdiy;
 
@@ -69,11 +69,16 @@ __global__ void __launch_bounds__(256) gemm_rr_k(const half* __restrict__ A, con
 
 extern "C" {
 
+int llmdiy_hgemm_swizzle_nn_path(const uint16_t* A, const uint16_t* B, const uint16_t* C, int M, int N, int K) {
+    if (M <= 0 || N <= 0 || K <= 0) return -1;
+    return (N % 8 == 0 && K % 8 == 0 && aligned16(A) && aligned16(B) && aligned16(C)) ? 1 : 0;
+}
+
 int llmdiy_hgemm_swizzle_nn(uint16_t* A, uint16_t* B, uint16_t* C, int M, int N, int K, void* stream) {
-    if (M <= 0 || N <= 0 || K <= 0) return (int)cudaErrorInvalidValue;
-    // tcgen05 path (B staged MN-major by TMA) where the layout allows it
-    if (N % 64 == 0 && K % 8 == 0 && aligned16(A) && aligned16(B) && aligned16(C))
-        return llmdiy_gemm_tc_kn(A, B, C, M, N, K, stream);
+    const int path = llmdiy_hgemm_swizzle_nn_path(A, B, C, M, N, K);
+    if (path < 0) return (int)cudaErrorInvalidValue;
+    // tcgen05 path (B staged MN-major by TMA; columns past N read as zeros, the store masks them)
+    if (path == 1) return llmdiy_gemm_tc_kn(A, B, C, M, N, K, stream);
     // any other shape: CUDA-core tiles
     dim3 grid((N + 63) / 64, (M + 63) / 64);
     gemm_rr_k<<<grid, 256, 0, S(stream)>>>(reinterpret_cast<const half*>(A), reinterpret_cast<const half*>(B),
@@ -94,18 +99,10 @@ int llmdiy_flash_attn_tuned_A(uint16_t* Q, uint16_t* K, uint16_t* V, uint16_t* O
     const half* k = reinterpret_cast<const half*>(K) + kb;
     const half* v = reinterpret_cast<const half*>(V) + vb;
     half* o = reinterpret_cast<half*>(O) + ob;
-    // 16-byte vector accesses: every row start must be 16-byte aligned
-    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-    if (!al(q) || !al(k) || !al(v) || !al(o)) return (int)cudaErrorInvalidValue;
-    // tensor-core flash attention (one head: grid.y = 1, head offset 0)
-    static std::once_flag attr;
-    std::call_once(attr, [] {
-        cudaFuncSetAttribute(flash_prefill_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sizeof(FlashPrefillSmem));
-    });
-    flash_prefill_k<<<dim3((N + kFpRows - 1) / kFpRows, 1), kFpThreads, sizeof(FlashPrefillSmem), S(stream)>>>(
-        q, k, v, o, N, 0, stride_Q, stride_KV);
-    return (int)cudaGetLastError();
+    // TMA row addressing: every row start must be 16-byte aligned
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return (int)cudaErrorInvalidValue;
+    // tcgen05 flash attention of one head: query row i at position i attends key rows 0..i
+    return flash_tc_causal(q, stride_Q, k, v, stride_KV, N, o, stride_Q, N, 0, 1, S(stream));
 }
 
 }  // extern "C"

@@ -1,7 +1,7 @@
 // prefill_tc.cu — the prompt forward (QwenEngine::prefill, qwen_infer.cu:372-611)
 // on the tensor cores: per layer
 //   RMSNorm(ln_1) rows -> QKV GEMM [epilogue: bias, RoPE, K/V appended to the
-//   cache, Q kept] -> causal flash attention over the cache (flash_prefill.cuh)
+//   cache, Q kept] -> causal flash attention over the cache (flash_tc.cuh)
 //   -> o_proj GEMM [epilogue:
 //   residual add] -> RMSNorm(ln_2) rows -> w1|w2 GEMM [epilogue: SwiGLU] ->
 //   c_proj GEMM [epilogue: residual add].
@@ -15,7 +15,6 @@
 #include <mutex>
 
 #include "decode.h"
-#include "flash_prefill.cuh"
 #include "flash_tc.cuh"
 #include "gemm_tc_host.h"
 #include "ops.cuh"
@@ -72,13 +71,27 @@ struct EpiQKV {
 
 }  // namespace
 
-int prefill_tc(const PrefillArgs& p, const int* tokens_dev, int n, int p0, cudaStream_t st) {
-    int rc = 0;
-    cudaError_t e;
+int flash_tc_causal(const half* q, int ldq, const half* k, const half* v, int ldkv, int kv_rows, half* o, int ldo,
+                    int n, int p0, int heads, cudaStream_t st) {
     static std::once_flag attr;
     std::call_once(attr, [] {
         cudaFuncSetAttribute(flash_tc_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(FlashTcSmem));
     });
+    CUtensorMap tq, tk, tv;
+    const int width = heads * kHeadDim;
+    if (!make_kmajor_map(&tq, q, n, width, ldq, kFtRows) || !make_kmajor_map(&tk, k, kv_rows, width, ldkv, kFtKeys) ||
+        !make_kmajor_map(&tv, v, kv_rows, width, ldkv, kFtKeys))
+        return (int)cudaErrorInvalidValue;
+    int* err = gemm_err_word();
+    if (!err) return (int)cudaErrorMemoryAllocation;
+    flash_tc_k<<<dim3((n + kFtRows - 1) / kFtRows, heads), kFtThreads, sizeof(FlashTcSmem), st>>>(tq, tk, tv, o, ldo,
+                                                                                                  n, p0, err);
+    return (int)cudaGetLastError();
+}
+
+int prefill_tc(const PrefillArgs& p, const int* tokens_dev, int n, int p0, cudaStream_t st) {
+    int rc = 0;
+    cudaError_t e;
     for (int c0 = 0; c0 < n; c0 += kPrefillChunk) {
         const int m = n - c0 < kPrefillChunk ? n - c0 : kPrefillChunk;
         const int pos0 = p0 + c0;
@@ -91,13 +104,8 @@ int prefill_tc(const PrefillArgs& p, const int* tokens_dev, int n, int p0, cudaS
             rc = launch_gemm_tc(p.xn, kHidden, L.qkv_w, kHidden, m, 3 * kHidden, kHidden,
                                 EpiQKV{L.qkv_b, p.q, kcl, vcl, pos0}, st);
             if (rc) return rc;
-            CUtensorMap tq, tk, tv;
-            if (!make_kmajor_map(&tq, p.q, m, kHidden, kHidden, kFtRows) ||
-                !make_kmajor_map(&tk, kcl, p.max_seqlen, kHidden, kHidden, kFtKeys) ||
-                !make_kmajor_map(&tv, vcl, p.max_seqlen, kHidden, kHidden, kFtKeys))
-                return (int)cudaErrorInvalidValue;
-            flash_tc_k<<<dim3((m + kFtRows - 1) / kFtRows, kHeads), kFtThreads, sizeof(FlashTcSmem), st>>>(
-                tq, tk, tv, p.att, m, pos0, gemm_err_word());
+            rc = flash_tc_causal(p.q, kHidden, kcl, vcl, kHidden, p.max_seqlen, p.att, kHidden, m, pos0, kHeads, st);
+            if (rc) return rc;
             rc = launch_gemm_tc(p.att, kHidden, L.proj_w, kHidden, m, kHidden, kHidden, EpiResidual{p.x}, st);
             if (rc) return rc;
             rmsnorm_rows_k<<<m, 256, 0, st>>>(p.xn, p.x, L.ln2);

@@ -87,6 +87,7 @@ def lib() -> ctypes.CDLL:
         "llmdiy_argmax": [P, P, I, P],
         "llmdiy_hgemv": [P, P, P, I, I, P],
         "llmdiy_hgemm_swizzle_nn": [P, P, P, I, I, I, P],
+        "llmdiy_hgemm_swizzle_nn_path": [P, P, P, I, I, I],
         "llmdiy_flash_attn_tuned_A": [P, P, P, P, I, I, I, I, I, I, I, I, P],
         "llmdiy_gather_q_from_qkv": [P, P, I, I, I, P],
         "llmdiy_gather_kv_from_cache": [P, P, I, I, I, P],
@@ -278,6 +279,11 @@ def hgemv(A, B, C, N, K, stream=None):
 
 def hgemm_swizzle_nn(A, B, C, M, N, K, stream=None):
     _check(lib().llmdiy_hgemm_swizzle_nn(_p(A), _p(B), _p(C), M, N, K, _p(stream)), "hgemm_swizzle_nn")
+
+
+def hgemm_swizzle_nn_path(A, B, C, M, N, K) -> int:
+    """Which kernel hgemm_swizzle_nn runs for these arguments: 1 tcgen05, 0 CUDA cores, -1 invalid."""
+    return int(lib().llmdiy_hgemm_swizzle_nn_path(_p(A), _p(B), _p(C), M, N, K))
 
 
 def flash_attn_tuned_A(Q, K, V, O, N, QKV_head, stride_Q, stride_KV, K_ofs=-1, V_ofs=-1, Q_ofs=-1, O_ofs=-1,

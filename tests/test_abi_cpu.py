@@ -167,3 +167,15 @@ def test_oracle_random_writer_matches_library():
     assert open(p1, "rb").read() == open(p2, "rb").read()
     os.remove(p1)
     os.remove(p2)
+
+
+def test_hgemm_dispatch_rule():
+    """llmdiy_hgemm_swizzle_nn_path (host only): the tcgen05 kernel whenever a TMA descriptor can
+    address the row pitches (N, K multiples of 8 elements, 16-byte aligned pointers)."""
+    a = 1 << 20
+    assert L.hgemm_swizzle_nn_path(a, a, a, 2048, 5504, 2048) == 1
+    assert L.hgemm_swizzle_nn_path(a, a, a, 300, 200, 104) == 1
+    assert L.hgemm_swizzle_nn_path(a, a, a, 300, 200, 100) == 0
+    assert L.hgemm_swizzle_nn_path(a, a, a, 8, 12, 8) == 0
+    assert L.hgemm_swizzle_nn_path(a + 8, a, a, 64, 64, 64) == 0
+    assert L.hgemm_swizzle_nn_path(a, a, a, 0, 64, 64) == -1

@@ -164,17 +164,22 @@ def test_fd_v5_split(oracle, rng, ref, L_, stride):
         assert max_abs(host(O), host(rO)) < 1e-3
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (127, 6144, 2048), (300, 200, 100), (2048, 5504, 2048)])
-def test_hgemm_swizzle_nn(oracle, rng, M, N, K):
+@pytest.mark.parametrize("M,N,K,path", [(128, 128, 128, 1), (127, 6144, 2048, 1), (300, 200, 104, 1),
+                                         (77, 136, 2048, 1), (2048, 5504, 2048, 1), (300, 200, 100, 0)])
+def test_hgemm_swizzle_nn(oracle, rng, M, N, K, path):
+    """path 1: the tcgen05 kernel (ragged N: TMA zero-fills the columns past N, the store masks them);
+    path 0: K = 100 gives a row pitch of 200 bytes that no TMA descriptor can address."""
     A = refmath.h((rng.random((M, K)) - 0.5) * 0.1)
     B = refmath.h((rng.random((K, N)) - 0.5) * 0.1)
     dA, dB, C = dev(A), dev(B), zeros16(M * N)
+    assert L.hgemm_swizzle_nn_path(dA.data_ptr(), dB.data_ptr(), C.data_ptr(), M, N, K) == path
     L.hgemm_swizzle_nn(dA.data_ptr(), dB.data_ptr(), C.data_ptr(), M, N, K)
     assert max_abs(host(C).reshape(M, N), oracle.hgemm_kn(A, B)) < 2e-2
 
 
 @pytest.mark.parametrize("N", [1, 100, 257, 1000])
 def test_flash_attn_causal(oracle, rng, ref, N):
+    """The reference-signature launcher on the tcgen05 flash attention of the engine's prefill."""
     Q = refmath.h(rng.standard_normal(N * 128))
     K = refmath.h(rng.standard_normal(N * 128))
     V = refmath.h(rng.standard_normal(N * 128))
