@@ -1,16 +1,19 @@
 // decode_kernel.cu — the persistent bs1 decode kernel (QwenEngine::step,
 // framework_src/qwen_infer.cu:614-737, for many steps per launch).
 //
-// One CTA of 8 warps per SM.  Each CTA streams its share of every weight
-// matrix through an 8-slot ring of 24 KB shared-memory slots with 1-D bulk
-// copies (TMA).  Slot w belongs to warp w: the warp consumes chunks w, w+8,
-// w+16, ... of the CTA's chunk sequence, and right after draining a chunk its
-// lane 0 issues the copy of its next chunk (a cursor walks the same sequence
-// eight chunks ahead).  Weights never depend on activations, so those copies
-// run ahead across phase, layer and token boundaries and HBM keeps streaming
-// while the warps wait for activations.  A warp consumes two rows at a time
-// (fp32 FMA dot products against the activation held in registers or shared
-// memory), with the reference's small ops fused into the epilogues:
+// One CTA of 8 consumer warps and 1 producer warp per SM.  Each CTA streams
+// its share of every weight matrix through an 8-slot ring of 24 KB
+// shared-memory slots with 1-D bulk copies (TMA): chunk g of the CTA's chunk
+// sequence goes to slot g % 8.  The producer (one lane) issues chunk g as soon
+// as the consumers have released chunk g - 8 (an "empty" mbarrier per slot),
+// and prefetches a later chunk into L2.  Weights never depend on activations,
+// so those copies run ahead across phase, layer and token boundaries and HBM
+// keeps streaming while the consumers wait for activations.  A phase's units
+// (two weight rows each) are dealt round-robin to the 8 consumer warps, unit i
+// to warp i % 8, so the warps work through the ring in sequence order and the
+// oldest slots free up first; a warp consumes its unit's two rows (fp32 FMA dot
+// products against the activation held in registers or shared memory), with the
+// reference's small ops fused into the epilogues:
 //   QKV  : RMSNorm(ln_1) prologue; bias; RoPE; K/V append at row pos
 //   ATT  : 16 heads x 9 position splits; split 0 of a head merges the (m,l,o) partials
 //   O    : residual add
@@ -33,6 +36,8 @@ enum PhaseId { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_W12 = 3, PH_C = 4, PH_LM = 5
 constexpr int kMaxIM = 6144;
 constexpr int kQkvBiasUnits = 64;  // QKV units per CTA whose bias pairs are staged in shared memory
 constexpr uint32_t kPollLimit = 1u << 21;  // polls of one flag-carrying word or of the step barrier
+constexpr int kDecodeBlock = kDecodeThreads + 32;  // 8 consumer warps + the producer warp
+constexpr uint32_t kEmptyArrivals = 3;  // per chunk: one per unit, the last unit of a chunk tops up to 3
 
 struct __align__(128) Smem {
     uint8_t ring[kRingStages][kStageBytes];
@@ -44,11 +49,13 @@ struct __align__(128) Smem {
     float sm[kConsumerWarps], sl[kConsumerWarps];
     float red[32];
     unsigned long long wkey[kConsumerWarps];
-    uint64_t full[kRingStages];
+    uint64_t full[kRingStages];   // chunk landed (the producer's expect_tx + the copy's bytes)
+    uint64_t empty[kRingStages];  // chunk consumed (kEmptyArrivals per chunk from the consumer warps)
     LayerPtrs layers[kMaxLayers];  // copy of a.layers (read at every phase change)
     int range[5][4];               // per phase (qkv, o, w12, c, lm): this CTA's units [u0, u1), units per chunk, K
     float qbias[kQkvBiasUnits][2];  // this layer's QKV bias pairs of the CTA's QKV units (loaded ahead)
     volatile int fail;  // a consumer wait expired
+    volatile int stop;  // the consumers have left the step loop: the producer stops issuing
     int token;
     int last;
 };
@@ -67,54 +74,33 @@ __device__ __forceinline__ void fma2_f16(float& acc0, float& acc1, uint32_t w, u
 }
 
 
-// The three units (six rows of K = 2048) of a chunk against the lane's
-// activation slice in registers, all rows at once for load/FMA parallelism,
-// then a transposing butterfly (9 shuffles for 6 sums instead of 30): lane
-// 8j ends with unit j's two dot products (rows 2j, 2j+1).  Rows past the
-// chunk's units read stale slot data and are ignored.
-__device__ __forceinline__ void dot6_regs(const half* buf, const uint32_t* xh, int lane, float& s0, float& s1) {
-    float a[6][2];
-#pragma unroll
-    for (int r = 0; r < 6; ++r) a[r][0] = a[r][1] = 0.f;
+// The two rows (a unit) of K = 2048 starting at `r0` against the lane's
+// activation slice in registers (lane holds elements 256 j + 8 lane .. +7),
+// then a transposing butterfly: every lane ends with both sums.
+__device__ __forceinline__ void dot2_regs(const half* r0, const uint32_t* xh, int lane, float& s0, float& s1) {
+    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        uint4 w[6];
-#pragma unroll
-        for (int r = 0; r < 6; ++r) w[r] = *reinterpret_cast<const uint4*>(buf + r * kHidden + 256 * j + 8 * lane);
-#pragma unroll
-        for (int r = 0; r < 6; ++r) {
-            fma2_f16(a[r][0], a[r][1], w[r].x, xh[4 * j + 0]);
-            fma2_f16(a[r][0], a[r][1], w[r].y, xh[4 * j + 1]);
-            fma2_f16(a[r][0], a[r][1], w[r].z, xh[4 * j + 2]);
-            fma2_f16(a[r][0], a[r][1], w[r].w, xh[4 * j + 3]);
-        }
+        const uint4 w0 = *reinterpret_cast<const uint4*>(r0 + 256 * j + 8 * lane);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(r0 + kHidden + 256 * j + 8 * lane);
+        fma2_f16(a0, a1, w0.x, xh[4 * j + 0]);
+        fma2_f16(b0, b1, w1.x, xh[4 * j + 0]);
+        fma2_f16(a0, a1, w0.y, xh[4 * j + 1]);
+        fma2_f16(b0, b1, w1.y, xh[4 * j + 1]);
+        fma2_f16(a0, a1, w0.z, xh[4 * j + 2]);
+        fma2_f16(b0, b1, w1.z, xh[4 * j + 2]);
+        fma2_f16(a0, a1, w0.w, xh[4 * j + 3]);
+        fma2_f16(b0, b1, w1.w, xh[4 * j + 3]);
     }
-    float v[8];
+    const float v0 = a0 + a1, v1 = b0 + b1;
+    // lanes < 16 keep row 0 and send row 1, lanes >= 16 the other way round: one shuffle halves both
+    const bool hi = lane & 16;
+    float t = (hi ? v1 : v0) + __shfl_xor_sync(0xffffffffu, hi ? v0 : v1, 16);
 #pragma unroll
-    for (int r = 0; r < 6; ++r) v[r] = a[r][0] + a[r][1];
-    v[6] = v[7] = 0.f;
-    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
-    float t[4], u[2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float send = b4 ? v[i] : v[i + 4], keep = b4 ? v[i + 4] : v[i];
-        t[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const float send = b3 ? t[i] : t[i + 2], keep = b3 ? t[i + 2] : t[i];
-        u[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-    float w;
-    {
-        const float send = b2 ? u[0] : u[1], keep = b2 ? u[1] : u[0];
-        w = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-    w += __shfl_xor_sync(0xffffffffu, w, 2);
-    w += __shfl_xor_sync(0xffffffffu, w, 1);
-    // lane l now holds row 4*b4 + 2*b3 + b2; the partner row of a unit sits 4 lanes up
-    s0 = w;
-    s1 = __shfl_down_sync(0xffffffffu, w, 4);
+    for (int m = 8; m >= 1; m >>= 1) t += __shfl_xor_sync(0xffffffffu, t, m);
+    const float o = __shfl_xor_sync(0xffffffffu, t, 16);
+    s0 = hi ? o : t;
+    s1 = hi ? t : o;
 }
 
 // fp32-accumulated dot products of two weight rows (a unit) of any K against
@@ -255,64 +241,50 @@ struct Tags {
     }
 };
 
-// ------------------------------------------------------------------ weight feed
-// Walks this CTA's chunk sequence: per step, per layer the chunks of qkv_w,
-// proj_w, w12, cproj, then (unless skip_lm) lm_head.  Chunk i of the
-// sequence goes to ring slot i % 8.
-// Producer side of a warp's ring slot: a cursor over the CTA's chunk schedule
-// (DecodeArgs::feed_tbl), visiting the chunks this warp owns (index = warp
-// mod 8) in order across layers, phases and steps.  The table entry of the
-// next chunk is loaded one issue ahead, so issuing costs two instructions.
-// A second cursor, a.l2_ahead owned chunks further on, prefetches into L2
-// so that HBM keeps streaming while the ring is full.
-struct Cursor {
-    int i, step;    // index in the step's schedule, step
-    uint2 ent;      // its table entry
-    bool done;
-};
-struct Feed {
-    int E;          // chunks per step of this CTA
-    uint32_t g;     // global index of cur (step * E + i): the ring phase parity is (g >> 3) & 1
-    uint32_t last;  // global index of the last chunk issued (0xffffffff: none)
-    Cursor cur, pre;
-};
-
-__device__ __forceinline__ void cursor_step(const DecodeArgs& a, Cursor& c, int E, int by) {
-    c.i += by;
-    while (c.i >= E) { c.i -= E; c.step++; }
-    c.done = c.step >= a.n_steps;
-    if (!c.done) c.ent = __ldg(a.feed_tbl + (size_t)blockIdx.x * a.feed_stride + c.i);
-}
-
-__device__ __forceinline__ void feed_init(const DecodeArgs& a, Feed& f, int warp) {
+// ------------------------------------------------------------------ producer
+// One lane of the producer warp walks this CTA's chunk sequence (DecodeArgs::feed_tbl: per step,
+// per layer the chunks of qkv_w, proj_w, w12, cproj, then unless skip_lm lm_head's) and copies
+// chunk g into ring slot g % 8 once the consumers have released chunk g - 8 there.  With each
+// copy it prefetches chunk g + 8 * l2_ahead into L2, so HBM keeps streaming while the ring is
+// full.  Every wait is bounded and gives up when the consumers have stopped or failed; before
+// returning, the producer waits (bounded) for its copies in flight, so none lands in the shared
+// memory of an exited CTA.
+__device__ void producer(const DecodeArgs& a, Smem& s) {
+    if ((threadIdx.x & 31) != 0) return;
     const int b = blockIdx.x;
-    f.E = a.feed_cnt[2 * b] + (a.skip_lm ? 0 : a.feed_cnt[2 * b + 1]);
-    f.g = (uint32_t)warp;
-    f.last = 0xffffffffu;
-    f.cur.i = 0;
-    f.cur.step = 0;
-    f.cur.done = true;
-    f.pre = f.cur;
-    if (f.E <= 0) return;
-    cursor_step(a, f.cur, f.E, warp);
-    f.pre = f.cur;
-    if (a.l2_ahead > 0) cursor_step(a, f.pre, f.E, kRingStages * a.l2_ahead);
-    else f.pre.done = true;
-}
-
-// Issue the copy of the next chunk owned by `warp` (lane 0 only).
-__device__ __forceinline__ void feed_issue_next(const DecodeArgs& a, Feed& f, Smem& s, int warp, uint64_t pol) {
-    if (f.cur.done) return;
-    const uint32_t bytes = f.cur.ent.y;
-    mbar_arrive_expect_tx(&s.full[warp], bytes);
-    bulk_g2s(s.ring[warp], a.wbase + (size_t)f.cur.ent.x * 16u, bytes, &s.full[warp], pol);
-    f.last = f.g;
-    f.g += kRingStages;
-    cursor_step(a, f.cur, f.E, kRingStages);
-    if (!f.pre.done) {
-        bulk_prefetch_l2(a.wbase + (size_t)f.pre.ent.x * 16u, f.pre.ent.y);
-        cursor_step(a, f.pre, f.E, kRingStages);
+    const int E = a.feed_cnt[2 * b] + (a.skip_lm ? 0 : a.feed_cnt[2 * b + 1]);
+    const uint2* tbl = a.feed_tbl + (size_t)b * a.feed_stride;
+    const uint32_t total = (uint32_t)E * (uint32_t)a.n_steps;
+    const uint32_t ahead = (uint32_t)(kRingStages * a.l2_ahead);
+    const uint64_t pol = l2_policy_evict_first();
+    int i = 0, ip = (int)(ahead % (uint32_t)(E > 0 ? E : 1));  // table index of chunk g and of chunk g + ahead
+    uint32_t g = 0;
+    for (; g < total; ++g) {
+        const int slot = (int)(g & (kRingStages - 1));
+        if (g >= (uint32_t)kRingStages) {
+            // use k = g / 8 of the slot needs use k - 1 released
+            const uint32_t par = ((g >> 3) - 1) & 1;
+            bool ok = false;
+            for (uint32_t it = 0; it < kSpinLimit; ++it) {
+                if (mbar_try_wait(&s.empty[slot], par)) { ok = true; break; }
+                if (s.stop || s.fail) break;
+                if (it > 64) __nanosleep(32);
+            }
+            if (!ok) break;  // the consumers left (end of the launch, a stop id or a failure)
+        }
+        const uint2 ent = tbl[i];
+        mbar_arrive_expect_tx(&s.full[slot], ent.y);
+        bulk_g2s(s.ring[slot], a.wbase + (size_t)ent.x * 16u, ent.y, &s.full[slot], pol);
+        if (ahead && g + ahead < total) {
+            const uint2 pe = tbl[ip];
+            bulk_prefetch_l2(a.wbase + (size_t)pe.x * 16u, pe.y);
+        }
+        if (++i == E) i = 0;
+        if (++ip == E) ip = 0;
     }
+    // drain: the last copy issued into each slot has landed
+    for (uint32_t k = g > (uint32_t)kRingStages ? g - kRingStages : 0; k < g; ++k)
+        (void)mbar_wait(&s.full[k & (kRingStages - 1)], (k >> 3) & 1);
 }
 
 // ------------------------------------------------------------------ consumers
@@ -443,79 +415,71 @@ __device__ __forceinline__ void epilogue(int ph, const DecodeArgs& a, const Smem
     }
 }
 
-// Consume this CTA's chunks of one weight matrix (rows in units of two).
-// A wait that expires marks `bad` and the remaining chunks are skipped.
-// Phases run through one call site so the kernel's code stays small enough
-// for the instruction caches (the phase id selects range, dot and epilogue).
+// Consume this CTA's units of one weight matrix (two rows each): unit i of the phase goes to
+// warp i % 8, so the warps take the ring's chunks in sequence order and release the oldest slot
+// first.  Each unit's warp releases it on the chunk's "empty" barrier (kEmptyArrivals per chunk:
+// the last unit of a chunk adds the arrivals of the units the chunk does not have).  A wait that
+// expires marks `bad` and the remaining units are skipped.  Phases run through one call site so
+// the kernel's code stays small enough for the instruction caches (the phase id selects range,
+// dot and epilogue).
 __device__ __forceinline__ void gemv_phase(int PH, const DecodeArgs& a, Smem& s, StepCtx& c, uint32_t& chunk,
-                                           const uint32_t* xr, int warp, int lane, bool& bad, Feed& feed,
-                                           uint64_t pol) {
+                                           const uint32_t* xr, int warp, int lane, bool& bad) {
     const int R = PH == PH_LM ? 4 : PH == PH_C ? 3 : PH == PH_W12 ? 2 : PH == PH_O ? 1 : 0;
     const int u0 = s.range[R][0], u1 = s.range[R][1], CH = s.range[R][2], K = s.range[R][3];
-    unsigned long long pw = 0, pc = 0, pi = 0;  // per-chunk cycle sums (profiling only)
-    unsigned long long pmaxw = 0;  // longest single chunk wait (profiling only)
-    for (int cu = u0; cu < u1; cu += CH, ++chunk) {
-        if ((int)(chunk & (kRingStages - 1)) != warp) continue;
-        const int nun = (u1 - cu) < CH ? (u1 - cu) : CH;
+    unsigned long long pw = 0, pc = 0;  // per-unit cycle sums (profiling only)
+    unsigned long long pmaxw = 0;       // longest single wait (profiling only)
+    const int nu = u1 - u0;
+    const uint32_t c0 = chunk;
+    chunk = c0 + (uint32_t)((nu + CH - 1) / CH);
+    for (int i = warp; i < nu; i += kConsumerWarps) {
+        const int j = CH == 1 ? i : i / CH, r = i - j * CH;  // chunk of the phase, unit within it
+        const uint32_t g = c0 + (uint32_t)j;
+        const int slot = (int)(g & (kRingStages - 1));
         if (bad || s.fail) continue;
         const unsigned long long t0 = a.prof_prod ? (unsigned long long)clock64() : 0ull;
-        if (!mbar_wait(&s.full[warp], (chunk >> 3) & 1, &s.fail)) {
+        if (!mbar_wait(&s.full[slot], (g >> 3) & 1, &s.fail)) {
             if (lane == 0) record_error(a.ctl, kErrRingTimeout, PH);
             s.fail = 1;
             bad = true;
             continue;
         }
         const unsigned long long t1 = a.prof_prod ? (unsigned long long)clock64() : 0ull;
-        // the unit whose epilogue this lane runs: lane 8j after dot6_regs, lane j after dot2_smem
-        const int ej = PH == PH_C ? (lane < nun ? lane : -1) : (((lane & 7) == 0 && (lane >> 3) < nun) ? lane >> 3 : -1);
-        const half* buf = reinterpret_cast<const half*>(s.ring[warp]);
-        float r0s = 0.f, r1s = 0.f;  // the epilogue lane's two dot products
-        if (PH == PH_C) {
-#pragma unroll 1
-            for (int j = 0; j < nun; ++j) {
-                const half* r0 = buf + (size_t)j * 2 * K;
-                float s0, s1;
-                dot2_smem(r0, r0 + K, s.act, K, lane, s0, s1);
-                if (lane == j) { r0s = s0; r1s = s1; }
-            }
-        } else {
-            dot6_regs(buf, xr, lane, r0s, r1s);
-        }
-        // QKV: the bias pair of that unit, read after the dot products (read
-        // before them, it put about 1.5 us per layer on the critical path)
+        const half* rows = reinterpret_cast<const half*>(s.ring[slot]) + (size_t)r * 2 * K;
+        float s0, s1;
+        if (PH == PH_C) dot2_smem(rows, rows + K, s.act, K, lane, s0, s1);
+        else dot2_regs(rows, xr, lane, s0, s1);
+        const int u = u0 + i;
+        // QKV: the unit's bias pair, read after the dot products (read before them, it put about
+        // 1.5 us per layer on the critical path)
         float b0 = 0.f, b1 = 0.f;
-        if (PH == PH_QKV) {
-            if (ej >= 0) {
-                const int u = cu + ej;
-                if (u1 - u0 <= kQkvBiasUnits) {  // staged by the QKV prologue
-                    b0 = s.qbias[u - u0][0];
-                    b1 = s.qbias[u - u0][1];
-                } else {
-                    const int sec = u / (kHidden / 2), v = u % (kHidden / 2);
-                    const int i1 = sec * kHidden + (v / 64) * kHeadDim + (v % 64);
-                    b0 = h2f(c.bias[i1]);
-                    b1 = h2f(c.bias[i1 + 64]);
-                }
+        if (PH == PH_QKV && lane == 0) {
+            if (nu <= kQkvBiasUnits) {  // staged by the QKV prologue
+                b0 = s.qbias[i][0];
+                b1 = s.qbias[i][1];
+            } else {
+                const int sec = u / (kHidden / 2), v = u % (kHidden / 2);
+                const int i1 = sec * kHidden + (v / 64) * kHeadDim + (v % 64);
+                b0 = h2f(c.bias[i1]);
+                b1 = h2f(c.bias[i1 + 64]);
             }
         }
-        if (ej >= 0) epilogue(PH, a, s, c, cu + ej, r0s, r1s, b0, b1);
-        __syncwarp();
-        const unsigned long long t2 = a.prof_prod ? (unsigned long long)clock64() : 0ull;
-        // the slot is drained: stream this warp's next chunk into it
-        if (lane == 0) feed_issue_next(a, feed, s, warp, pol);
+        if (lane == 0) {
+            epilogue(PH, a, s, c, u, s0, s1, b0, b1);
+            // every lane's reads of the slot are done (the butterfly consumed them): release it
+            const int nun = nu - j * CH < CH ? nu - j * CH : CH;
+            mbar_arrive_cnt(&s.empty[slot], r == nun - 1 ? kEmptyArrivals - (uint32_t)nun + 1u : 1u);
+        }
         if (a.prof_prod) {
             pw += t1 - t0;
             pmaxw = (t1 - t0) > pmaxw ? (t1 - t0) : pmaxw;
-            pc += t2 - t1;
-            pi += (unsigned long long)clock64() - t2;
+            pc += (unsigned long long)clock64() - t1;
         }
     }
     if (a.prof_prod && lane == 0) {
-        // per CTA, phase and warp: SM cycles waiting for chunks, computing, issuing; the longest wait
+        // per CTA, phase and warp: SM cycles waiting for chunks, computing; the longest wait
         unsigned long long* q = a.prof_prod + (((size_t)blockIdx.x * 6 + PH) * kConsumerWarps + warp) * 4;
         atomicAdd(q, pw);  // reductions: no round trip on the phase's critical path
         atomicAdd(q + 1, pc);
-        atomicAdd(q + 2, pi);
         atomicMax(q + 3, pmaxw);
     }
 }
@@ -767,12 +731,6 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
     const Tags tags{a.flag_base, a.NL};
     bool bad = false;
     int np = 0;  // probe index
-    const uint64_t pol = l2_policy_evict_first();
-    Feed feed{};
-    if (lane == 0) {
-        feed_init(a, feed, warp);
-        feed_issue_next(a, feed, s, warp, pol);  // this warp's first chunk
-    }
     for (int step = 0; step < a.n_steps; ++step) {
         c.pos = a.pos0 + step;
         c.step = step;
@@ -850,7 +808,7 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
             c.tag = tags(step, l, ph == PH_QKV ? LL_QKV : ph == PH_O ? LL_XO : ph == PH_W12 ? LL_ACT : LL_XC);
             c.best = 0ull;
             probe(a, tid, np);
-            gemv_phase(ph, a, s, c, chunk, xr, warp, lane, bad, feed, pol);
+            gemv_phase(ph, a, s, c, chunk, xr, warp, lane, bad);
         }
         if (failed) break;
         if (a.skip_lm) {
@@ -894,18 +852,20 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
         if (token == a.stop0 || token == a.stop1) break;
     }
     if (bad) record_error(a.ctl, kErrHeadMergeTimeout, -1);
-    // Drain: the last copy this warp issued must have landed before the CTA
-    // exits (waiting on an already-consumed chunk returns at once: no later
-    // copy went to this slot).
-    if (lane == 0 && feed.last != 0xffffffffu) mbar_wait(&s.full[warp], (feed.last >> 3) & 1);
+    // the producer stops issuing once it sees this (and drains its copies in flight)
+    if (tid == 0) s.stop = 1;
 }
 
-__global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kDecodeBlock, 1) decode_kernel(const DecodeArgs a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>(smem_raw);
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kRingStages; ++i) mbar_init(&s.full[i], 1);
+        for (int i = 0; i < kRingStages; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.empty[i], kEmptyArrivals);
+        }
         s.fail = 0;
+        s.stop = 0;
         mbar_fence_init();
     }
     for (int i = threadIdx.x; i < a.NL * (int)(sizeof(LayerPtrs) / sizeof(uint64_t)); i += blockDim.x)
@@ -919,7 +879,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) decode_kernel(const DecodeA
         s.range[threadIdx.x][3] = r.K;
     }
     __syncthreads();
-    consumers(a, s);
+    // from here on the consumer warps synchronise on named barrier 1 (256 threads) only
+    if (threadIdx.x >= kDecodeThreads) producer(a, s);
+    else consumers(a, s);
 }
 
 }  // namespace
@@ -938,7 +900,7 @@ cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t stream) {
                                          (int)sizeof(Smem));
     if (e != cudaSuccess) return e;
     void* args[] = {const_cast<DecodeArgs*>(&a)};
-    return cudaLaunchCooperativeKernel((const void*)decode_kernel, dim3(grid), dim3(kDecodeThreads), args,
+    return cudaLaunchCooperativeKernel((const void*)decode_kernel, dim3(grid), dim3(kDecodeBlock), args,
                                        sizeof(Smem), stream);
 }
 
