@@ -447,7 +447,7 @@ def fd_op_leg(args, rank, world, local, pg):
         Vs = [torch.randn(Lc * FD_STRIDE, generator=g, device=dev).half() for _ in range(nset)]
         O = torch.empty(FD_HEADS * 128, dtype=torch.float16, device=dev)
         nb = L.fd_mh_work_bytes(Lc, FD_HEADS)
-        work = torch.empty((nb + 3) // 4, dtype=torch.float32, device=dev)
+        work = torch.zeros((nb + 3) // 4, dtype=torch.float32, device=dev)
         st = torch.cuda.Stream(device=dev)
 
         def ours():
@@ -502,7 +502,7 @@ def fd_op_leg(args, rank, world, local, pg):
     V = torch.randn(Lr * FD_STRIDE, generator=g, device=dev).half()
     O = torch.empty(FD_HEADS * 128, dtype=torch.float16, device=dev)
     nb = L.fd_mh_work_bytes(Lr, FD_HEADS)
-    work = torch.empty((nb + 3) // 4, dtype=torch.float32, device=dev)
+    work = torch.zeros((nb + 3) // 4, dtype=torch.float32, device=dev)
     st = torch.cuda.current_stream(dev)
     att_p2p = D.SplitKVAttention(pg.group.WORLD, FD_HEADS, FD_STRIDE, exchange="p2p") if world > 1 else None
 

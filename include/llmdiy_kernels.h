@@ -70,10 +70,13 @@ int llmdiy_gemm_tc_status(void);
  * head at qwen_infer.cu:650-677).  Q is [num_heads][128] fp16; K and V are the engine's cache layout,
  * row r of head h at r*stride + h*128 (stride >= num_heads*128, a multiple of 8); O is [num_heads][128].
  * Scale 1/sqrt(128), fp32 accumulation, fast-math exponentials like the reference.  `work` is caller
- * scratch of llmdiy_fd_mh_work_bytes(L, num_heads) bytes (device memory, 16-byte aligned); nothing is
+ * scratch of llmdiy_fd_mh_work_bytes(L, num_heads) bytes (device memory, 16-byte aligned, zero-filled once
+ * before its first use: its last word is the error word, which the kernels only set); nothing is
  * allocated.  A partial is 130 fp32: o[128] (unnormalised), m (max score), l (sum of e^{s-m}). */
 size_t llmdiy_fd_mh_work_bytes(int L, int num_heads);
-/* O = softmax(q k^T / sqrt(128)) v for every head over rows [0, L). */
+/* O = softmax(q k^T / sqrt(128)) v for every head over rows [0, L).  L <= 2048: one launch, a cluster of
+ * 8 CTAs per head merging through distributed shared memory (the workspace only carries the error word);
+ * longer caches: the persistent split kernel and a merge kernel. */
 int llmdiy_fd_multihead(const uint16_t* Q, const uint16_t* K, const uint16_t* V, uint16_t* O, int L, int stride,
                         int num_heads, float* work, size_t work_bytes, void* stream);
 /* One merged partial per head over rows [0, L) of this K/V shard: part is [num_heads][130] fp32. */
@@ -81,8 +84,8 @@ int llmdiy_fd_mh_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* 
                           int num_heads, float* part, float* work, size_t work_bytes, void* stream);
 /* Log-sum-exp merge of G shards' partials, parts = [G][num_heads][130] in shard order, into O. */
 int llmdiy_fd_mh_merge(const float* parts, int G, int num_heads, uint16_t* O, void* stream);
-/* After the stream is synchronised: 0, or -5 when a pipeline wait of the last call with this
- * workspace expired (its output is then not valid). */
+/* After the stream is synchronised: 0, or -5 when a pipeline wait of a call with this workspace expired
+ * since the last status query (that output is then not valid); the query clears the word. */
 int llmdiy_fd_mh_status(const float* work, int L, int num_heads);
 
 /* Multi-GPU exchange of the shards' partials over peer memory (no counterpart in the reference,

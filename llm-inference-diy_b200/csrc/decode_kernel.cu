@@ -325,6 +325,24 @@ __device__ bool grid_sync(const DecodeArgs& a, Smem& s, uint32_t& nbar, int tid,
     return !named_bar_or(1, 256, failed);
 }
 
+__device__ __forceinline__ void prefetch_l2_line(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+// As prefetch_l2_line, with the line marked to be evicted last: the small per-layer vectors on
+// the critical path (norm weights, QKV bias) stay in L2 while the weight stream (evict-first)
+// passes through it.
+__device__ __forceinline__ void prefetch_l2_keep(const void* p) {
+    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
+}
+// 16-byte load that keeps its L2 line evict-last (see prefetch_l2_keep).
+__device__ __forceinline__ uint4 ld_keep_u4(const void* p, uint64_t pol) {
+    uint4 v;
+    asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p), "l"(pol));
+    return v;
+}
+
 // Stage a residual-stream vector in shared memory (raw copy in xraw),
 // RMSNorm it with the reference tree and leave each lane's 64-element slice
 // of the normalised vector in xr.  The source is either a plain fp16 row (the
@@ -333,7 +351,7 @@ __device__ bool grid_sync(const DecodeArgs& a, Smem& s, uint32_t& nbar, int tid,
 __device__ bool load_norm(const DecodeArgs& a, const half* plain, const unsigned long long* ll, uint32_t tag,
                           const half* w, Smem& s, int tid, uint32_t* xr, bool bad, int& np,
                           float* stage_dst = nullptr, float stage_val = 0.f) {
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + tid * 8);  // in flight while polling
+    const uint4 wv = ld_keep_u4(w + tid * 8, l2_policy_evict_last());  // in flight while polling
     uint4 v;
     if (plain) {
         v = *reinterpret_cast<const uint4*>(plain + tid * 8);
@@ -484,9 +502,6 @@ __device__ __forceinline__ void gemv_phase(int PH, const DecodeArgs& a, Smem& s,
     }
 }
 
-__device__ __forceinline__ void prefetch_l2_line(const void* p) {
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
 
 // L2 prefetch, one line per thread, of what the critical path of the coming
 // phases reads from global memory besides flag words: the next layer's ln_1,
@@ -494,12 +509,29 @@ __device__ __forceinline__ void prefetch_l2_line(const void* p) {
 // the KV cache for the attention phase (rows before pos, written by earlier
 // steps).  With HBM saturated by the weight stream, a demand miss on these
 // would cost several microseconds on the critical path.
+// Every layer's norm weights and QKV bias (and ln_f), spread over the grid, into L2 as evict-last
+// lines at the start of a launch: together a few hundred KB that every step reads on its critical
+// path, and that a demand miss would fetch from an HBM saturated by the weight stream.
+__device__ void prefetch_small_vectors(const DecodeArgs& a, const Smem& s, int tid) {
+    constexpr int kLinesPerLayer = (kHidden * 2 + kHidden * 2 + 3 * kHidden * 2) / 128;  // ln_1, ln_2, qkv_b
+    const int total = a.NL * kLinesPerLayer + kHidden * 2 / 128;
+    for (int i = blockIdx.x * kDecodeThreads + tid; i < total; i += gridDim.x * kDecodeThreads) {
+        const int l = i / kLinesPerLayer, j = i % kLinesPerLayer;
+        if (l >= a.NL) {
+            prefetch_l2_keep(a.lnf + (size_t)(i - a.NL * kLinesPerLayer) * 64);
+        } else {
+            const LayerPtrs& L = s.layers[l];
+            const half* p = j < 32 ? L.ln1 + j * 64 : j < 64 ? L.ln2 + (j - 32) * 64 : L.qkv_b + (j - 64) * 64;
+            prefetch_l2_keep(p);
+        }
+    }
+}
 __device__ void prefetch_norms(const DecodeArgs& a, const Smem& s, int l, int tid) {
     const LayerPtrs& N = s.layers[l + 1 < a.NL ? l + 1 : 0];
-    if (tid < 32) prefetch_l2_line(N.ln1 + tid * 64);
-    else if (tid < 64) prefetch_l2_line(N.ln2 + (tid - 32) * 64);
-    else if (tid < 160) prefetch_l2_line(N.qkv_b + (tid - 64) * 64);
-    else if (tid < 192 && l + 1 == a.NL) prefetch_l2_line(a.lnf + (tid - 160) * 64);
+    if (tid < 32) prefetch_l2_keep(N.ln1 + tid * 64);
+    else if (tid < 64) prefetch_l2_keep(N.ln2 + (tid - 32) * 64);
+    else if (tid < 160) prefetch_l2_keep(N.qkv_b + (tid - 64) * 64);
+    else if (tid < 192 && l + 1 == a.NL) prefetch_l2_keep(a.lnf + (tid - 160) * 64);
 }
 __device__ void prefetch_kv_rows(const DecodeArgs& a, int l, int pos, int tid) {
     const int b = blockIdx.x;
@@ -731,6 +763,7 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
     const Tags tags{a.flag_base, a.NL};
     bool bad = false;
     int np = 0;  // probe index
+    prefetch_small_vectors(a, s, tid);
     for (int step = 0; step < a.n_steps; ++step) {
         c.pos = a.pos0 + step;
         c.step = step;

@@ -11,6 +11,13 @@
 // fp16 output or into one fp32 partial per head — the form the multi-GPU path
 // exchanges (over peer memory with fd_p2p_merge_k, or by an NCCL all-gather)
 // before the final merge of the shards' partials.
+//
+// Short caches (L <= 2048 rows) take a single launch instead: one thread-block
+// cluster of 8 CTAs per head (fd_cluster_k), each CTA loading its share of the
+// head's rows in 64-row TMA tiles at once and reducing them to a partial, then
+// CTA 0 of the cluster merging the 8 partials through distributed shared
+// memory.  No global scratch, no memset, no second kernel.
+#include <cooperative_groups.h>
 #include <cuda.h>
 #include <algorithm>
 #include <cstring>
@@ -223,6 +230,162 @@ __global__ void __launch_bounds__(kFdThreads, 1)
     }
 }
 
+// ------------------------------------------------------------------ short caches: one cluster per head
+constexpr int kFcCluster = 8;                                     // CTAs per head (portable cluster size)
+constexpr int kFcMaxTiles = 4;                                    // 64-row tiles per CTA
+constexpr int kFcMaxRows = kFcCluster * kFcMaxTiles * kFdRows;    // 2048 rows per head at most
+constexpr int kFcThreads = 256;
+
+// Shared memory: this header, then the CTA's T K tiles and T V tiles (T = R / 64, sized at launch so
+// that short caches leave room for more CTAs per SM).
+struct __align__(1024) FcSmem {
+    uint64_t full[kFcMaxTiles];
+    float so[kFcThreads / 32][kFdHeadDim];
+    float sm[kFcThreads / 32], sl[kFcThreads / 32];
+    float po[kFdHeadDim];  // this CTA's partial: o (unnormalised), then m and l
+    float pm, pl;
+};
+constexpr size_t kFcHeader = (sizeof(FcSmem) + 1023) / 1024 * 1024;
+
+// Cluster h (CTAs 8h .. 8h+7) attends head h; CTA rank r takes rows [r R, min(L, (r+1) R)), R a
+// multiple of 64.  All of its tiles are requested at once (one mbarrier each); warp w folds rows
+// w*8 .. w*8+7 of every tile (half-warp hw the rows of parity hw, 16-byte loads, online softmax),
+// then the CTA merges its 8 warps into a partial in shared memory.  After a cluster barrier, CTA 0
+// reads the 8 partials over distributed shared memory and writes the head's fp16 output; a second
+// barrier keeps every CTA's shared memory alive until then.  A copy wait that expires sets *err
+// (never cleared by the kernel) and the CTA still takes part in both barriers.
+__global__ void __cluster_dims__(kFcCluster, 1, 1) __launch_bounds__(kFcThreads, 1)
+    fd_cluster_k(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                 const half* __restrict__ Q, int L, int R, half* __restrict__ O, int* err) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    FcSmem& s = *reinterpret_cast<FcSmem*>(smem_raw);
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hw = lane >> 4, dl = (lane & 15) * 8;
+    const int rank = (int)cluster.block_rank(), h = blockIdx.x / kFcCluster;
+    const int r0 = rank * R, r1 = min(L, r0 + R);
+    const int T = r1 > r0 ? (r1 - r0 + kFdRows - 1) / kFdRows : 0;
+    half* ktiles = reinterpret_cast<half*>(smem_raw + kFcHeader);           // [R/64][64 * 128]
+    half* vtiles = ktiles + (size_t)(R / kFdRows) * kFdRows * kFdHeadDim;  // [R/64][64 * 128]
+    if (tid == 0) {
+        for (int t = 0; t < T; ++t) mbar_init(&s.full[t], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const uint64_t pol = l2_policy_evict_first();
+        for (int t = 0; t < T; ++t) {
+            mbar_arrive_expect_tx(&s.full[t], 2 * kFdTileBytes);
+            tma_load_2d_hint(ktiles + t * kFdRows * kFdHeadDim, &tk, h * kFdHeadDim, r0 + t * kFdRows, &s.full[t],
+                             pol);
+            tma_load_2d_hint(vtiles + t * kFdRows * kFdHeadDim, &tv, h * kFdHeadDim, r0 + t * kFdRows, &s.full[t],
+                             pol);
+        }
+    }
+    float q8[8];
+    unpack8(*reinterpret_cast<const uint4*>(Q + (size_t)h * kFdHeadDim + dl), q8);
+    const float scale = __frcp_rn(sqrtf((float)kFdHeadDim));
+    float m = -INFINITY, l = 0.f, o8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o8[e] = 0.f;
+    bool failed = false;
+    for (int t = 0; t < T; ++t) {
+        if (__syncthreads_or(!mbar_wait(&s.full[t], 0))) {
+            failed = true;
+            break;
+        }
+        const half* kt = ktiles + t * kFdRows * kFdHeadDim;
+        const half* vt = vtiles + t * kFdRows * kFdHeadDim;
+        const int nvalid = min(kFdRows, r1 - (r0 + t * kFdRows));
+        float sc[4];
+        uint4 vr[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int r = warp * 8 + 2 * j + hw;
+            float kf[8];
+            unpack8(*reinterpret_cast<const uint4*>(kt + r * kFdHeadDim + dl), kf);
+            vr[j] = *reinterpret_cast<const uint4*>(vt + r * kFdHeadDim + dl);
+            float d = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) d = __fmaf_rn(q8[e], kf[e], d);
+            sc[j] = d;
+        }
+#pragma unroll
+        for (int mk = 8; mk >= 1; mk >>= 1)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], mk);
+        float mx = m;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            sc[j] = warp * 8 + 2 * j + hw < nvalid ? sc[j] * scale : -INFINITY;
+            mx = fmaxf(mx, sc[j]);
+        }
+        if (mx != -INFINITY) {
+            const float corr = __expf(m - mx);
+            l *= corr;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o8[e] *= corr;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float p = __expf(sc[j] - mx);
+                l += p;
+                float vf[8];
+                unpack8(vr[j], vf);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) o8[e] = __fmaf_rn(p, vf[e], o8[e]);
+            }
+            m = mx;
+        }
+    }
+    combine_halfwarps(m, l, o8);
+    if (lane < 16) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s.so[warp][dl + e] = o8[e];
+    }
+    if (lane == 0) { s.sm[warp] = m; s.sl[warp] = l; }
+    __syncthreads();
+    if (tid < kFdHeadDim) {
+        float M = -INFINITY;
+        for (int w = 0; w < kFcThreads / 32; ++w) M = fmaxf(M, s.sm[w]);
+        float Ls = 0.f, acc = 0.f;
+        for (int w = 0; w < kFcThreads / 32; ++w) {
+            if (s.sm[w] == -INFINITY) continue;
+            const float f = __expf(s.sm[w] - M);
+            Ls += s.sl[w] * f;
+            acc = __fmaf_rn(f, s.so[w][tid], acc);
+        }
+        s.po[tid] = acc;
+        if (tid == 0) { s.pm = M; s.pl = Ls; }
+    }
+    cluster.sync();  // every CTA's partial is in its shared memory
+    if (rank == 0 && tid < kFdHeadDim) {
+        float pm[kFcCluster], pl[kFcCluster], po[kFcCluster];
+        float M = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kFcCluster; ++c) {
+            const FcSmem* peer = cluster.map_shared_rank(&s, c);
+            pm[c] = peer->pm;
+            pl[c] = peer->pl;
+            po[c] = peer->po[tid];
+            M = fmaxf(M, pm[c]);
+        }
+        float Ls = 0.f, acc = 0.f;
+#pragma unroll
+        for (int c = 0; c < kFcCluster; ++c) {
+            if (pm[c] == -INFINITY) continue;
+            const float f = __expf(pm[c] - M);
+            Ls = __fmaf_rn(pl[c], f, Ls);
+            acc = __fmaf_rn(f, po[c], acc);
+        }
+        O[(size_t)h * kFdHeadDim + tid] = f2h(acc * __frcp_rn(Ls));
+    }
+    cluster.sync();  // CTA 0 has read every peer's partial
+    if (failed && tid == 0) {
+        atomicExch(err, 1);
+        for (int t = 0; t < T; ++t) (void)mbar_wait(&s.full[t], 0);  // copies in flight land here first
+    }
+}
+
 // Merge of a head's S split partials (part = [H][S][130]) with 256 threads:
 // the weights e^{m_j - M} are computed once per partial, then thread group g
 // (threads g*128 .. g*128+127, one per dimension) sums partials j = g, g+2, ...
@@ -415,17 +578,16 @@ int check_args(const void* Q, const void* K, const void* V, int L, int stride, i
     return 0;
 }
 
-// Workspace: the split partials [H][S][130] fp32, then one error word
-// (cleared on the stream before every launch).
+// Workspace: the split partials [H][S][130] fp32, then one error word (zero-filled by the caller
+// before first use; a kernel only ever sets it, llmdiy_fd_mh_status reads and clears it).
 size_t work_floats(int H, int S) { return (size_t)H * S * kFdPart + 4; }
 
 int launch_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride, int H, float* work,
                     int S, int rows, uint16_t* O, float* out_part, cudaStream_t st) {
     CUtensorMap tk, tv;
     if (!make_map(&tk, K, L, stride) || !make_map(&tv, V, L, stride)) return (int)cudaErrorInvalidValue;
-    int* err = reinterpret_cast<int*>(work + (size_t)H * S * kFdPart);
-    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), st);
-    if (e != cudaSuccess) return (int)e;
+    int* err = reinterpret_cast<int*>(work + (size_t)H * S * kFdPart);  // set by the kernel, cleared by the status query
+    cudaError_t e;
     static std::once_flag attr;
     std::call_once(attr, [] {
         cudaFuncSetAttribute(fd_partials_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(FdSmem));
@@ -436,6 +598,26 @@ int launch_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int
     e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
     fd_merge_splits_k<<<H, kFdMergeThreads, 0, st>>>(work, S, reinterpret_cast<half*>(O), out_part);
+    return (int)cudaGetLastError();
+}
+
+// Short caches: one launch of fd_cluster_k, H clusters of 8 CTAs.  The error word (the workspace's
+// word after the partials) is only ever set by the kernels; the status query clears it.
+int launch_cluster(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride, int H, float* work,
+                   int S, uint16_t* O, cudaStream_t st) {
+    CUtensorMap tk, tv;
+    if (!make_map(&tk, K, L, stride) || !make_map(&tv, V, L, stride)) return (int)cudaErrorInvalidValue;
+    int* err = reinterpret_cast<int*>(work + (size_t)H * S * kFdPart);
+    static std::once_flag attr;
+    std::call_once(attr, [] {
+        cudaFuncSetAttribute(fd_cluster_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(kFcHeader + 2 * kFcMaxTiles * kFdTileBytes));
+    });
+    const int per = (L + kFcCluster - 1) / kFcCluster;
+    const int R = (per + kFdRows - 1) / kFdRows * kFdRows;
+    const size_t smem = kFcHeader + 2 * (size_t)(R / kFdRows) * kFdTileBytes;
+    fd_cluster_k<<<H * kFcCluster, kFcThreads, smem, st>>>(tk, tv, reinterpret_cast<const half*>(Q), L, R,
+                                                            reinterpret_cast<half*>(O), err);
     return (int)cudaGetLastError();
 }
 
@@ -456,6 +638,7 @@ extern "C" int llmdiy_fd_multihead(const uint16_t* Q, const uint16_t* K, const u
     plan(L, num_heads, &S, &rows);
     if (!O || !work || work_bytes < work_floats(num_heads, S) * sizeof(float)) return (int)cudaErrorInvalidValue;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (L <= kFcMaxRows) return launch_cluster(Q, K, V, L, stride, num_heads, work, S, O, st);
     return launch_partials(Q, K, V, L, stride, num_heads, work, S, rows, O, nullptr, st);
 }
 
@@ -482,8 +665,10 @@ extern "C" int llmdiy_fd_mh_status(const float* work, int L, int num_heads) {
     int S, rows;
     plan(L, num_heads, &S, &rows);
     int h = 0;
-    cudaError_t e = cudaMemcpy(&h, work + (size_t)num_heads * S * kFdPart, sizeof(int), cudaMemcpyDeviceToHost);
+    int* word = reinterpret_cast<int*>(const_cast<float*>(work) + (size_t)num_heads * S * kFdPart);
+    cudaError_t e = cudaMemcpy(&h, word, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return (int)e;
+    if (h) cudaMemset(word, 0, sizeof(int));  // the kernels only ever set it
     return h ? -5 : 0;
 }
 

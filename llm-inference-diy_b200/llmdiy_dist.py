@@ -160,7 +160,7 @@ class SplitKVAttention:
             return
         nb = L.fd_mh_work_bytes(rows, self.num_heads)
         if self._work is None or self._work.numel() * 4 < nb:
-            self._work = torch.empty((nb + 3) // 4, dtype=torch.float32, device=q.device)
+            self._work = torch.zeros((nb + 3) // 4, dtype=torch.float32, device=q.device)
         st = torch.cuda.current_stream(q.device).cuda_stream
         L.fd_mh_partials(q.data_ptr(), K.data_ptr(), V.data_ptr(), rows, self.stride, self.num_heads,
                          part.data_ptr(), self._work.data_ptr(), nb, stream=st)

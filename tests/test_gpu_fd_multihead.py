@@ -27,7 +27,7 @@ def _work(L_, H):
     t = torch()
     n = L.fd_mh_work_bytes(L_, H)
     assert n > 0
-    return t.empty((n + 3) // 4, dtype=t.float32, device="cuda"), n
+    return t.zeros((n + 3) // 4, dtype=t.float32, device="cuda"), n
 
 
 def _multihead(q, K, V, L_, H, stride):
@@ -40,8 +40,11 @@ def _multihead(q, K, V, L_, H, stride):
 
 
 @pytest.mark.parametrize("L_,H,stride", [(1024, 16, 2048), (1, 16, 2048), (63, 16, 2048), (65, 4, 512),
-                                         (1000, 16, 2048), (4097, 2, 256), (32768, 16, 2048)])
+                                         (1000, 16, 2048), (520, 16, 2048), (2048, 16, 2048), (2049, 8, 1024),
+                                         (4097, 2, 256), (32768, 16, 2048)])
 def test_fd_multihead_vs_oracle(oracle, rng, L_, H, stride):
+    """L <= 2048: the one-launch cluster kernel (L = 520 leaves three CTAs of each cluster without rows,
+    2048 fills all four tiles of every CTA); longer caches: the persistent split kernel + merge."""
     q, K, V = _inputs(rng, L_, H, stride)
     got, _ = _multihead(q, K, V, L_, H, stride)
     for h in range(H):
