@@ -107,7 +107,7 @@ struct DecodeArgs {
     const int* feed_cnt;      // [grid][2]
     int feed_stride;
     const uint8_t* wbase;
-    int l2_ahead;             // L2 prefetch distance in owned chunks beyond the ring (0 = off)
+    int l2_ahead;             // chunks prefetched into L2 ahead of the copy issued: 8 * l2_ahead (0 = off)
     // optional timing probes (null in production): per CTA and grid barrier,
     // %globaltimer at arrival and at release; per CTA the producer's time
     // blocked on a full ring and the consumers' time waiting for data.

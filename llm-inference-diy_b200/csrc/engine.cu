@@ -89,7 +89,7 @@ struct llmdiy_engine {
     uint2* feed_tbl = nullptr;  // decode kernel's per-CTA weight-chunk schedule of one step
     int* feed_cnt = nullptr;
     int feed_stride = 0;
-    int l2_ahead = 1;  // decode kernel's L2 look-ahead in owned chunks beyond the ring (env LLMDIY_L2_AHEAD)
+    int l2_ahead = 1;  // decode kernel: rings of chunks prefetched into L2 beyond the copy ring (env LLMDIY_L2_AHEAD)
     DecodeControl* ctl = nullptr;
     int* tokens_dev = nullptr;
     int* forced_dev = nullptr;
