@@ -353,17 +353,25 @@ __device__ bool load_norm(const DecodeArgs& a, const half* plain, const unsigned
                           float* stage_dst = nullptr, float stage_val = 0.f) {
     const uint4 wv = ld_keep_u4(w + tid * 8, l2_policy_evict_last());  // in flight while polling
     uint4 v;
+    uint32_t d[4];
     if (plain) {
         v = *reinterpret_cast<const uint4*>(plain + tid * 8);
     } else {
-        uint32_t d[4];
-        bad |= !ll_read<4>(ll + tid * 4, 1, tag, d);
-        v = make_uint4(d[0], d[1], d[2], d[3]);
+        // coalesced polls: thread t takes words t, t + 256, t + 512, t + 768
+        bad |= !ll_read<4>(ll + tid, kDecodeThreads, tag, d);
     }
     // the previous phase may still read xraw / xs: wait before overwriting
     if (named_bar_or(1, 256, bad)) return true;
     probe(a, tid, np);
-    *reinterpret_cast<uint4*>(s.xraw + tid * 8) = v;
+    if (plain) {
+        *reinterpret_cast<uint4*>(s.xraw + tid * 8) = v;
+    } else {
+        uint32_t* xw = reinterpret_cast<uint32_t*>(s.xraw);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xw[tid + k * kDecodeThreads] = d[k];
+        named_bar_sync(1, 256);
+        v = *reinterpret_cast<const uint4*>(s.xraw + tid * 8);
+    }
     const float r = rms_scale_regs2048(v, 1e-6f, s.red, tid, 1);  // v = this thread's eight elements
     float xf[8], wf[8], of[8];
     unpack8(v, xf);
@@ -793,10 +801,11 @@ __device__ void consumers(const DecodeArgs& a, Smem& s) {
                 if (failed) break;
                 probe(a, tid, np);
                 uint32_t d[4];
-                bad |= !ll_read<4>(a.ll_att + 4 * tid, 1, tags(step, l, LL_ATT), d);
+                bad |= !ll_read<4>(a.ll_att + tid, kDecodeThreads, tags(step, l, LL_ATT), d);
                 failed = named_bar_or(1, 256, bad);  // the previous phase is done with s.xs
                 if (failed) break;
-                *reinterpret_cast<uint4*>(s.xs + 8 * tid) = make_uint4(d[0], d[1], d[2], d[3]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) reinterpret_cast<uint32_t*>(s.xs)[tid + k * kDecodeThreads] = d[k];
                 named_bar_sync(1, 256);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
