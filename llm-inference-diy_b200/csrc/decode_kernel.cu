@@ -511,12 +511,6 @@ __device__ __forceinline__ void gemv_phase(int PH, const DecodeArgs& a, Smem& s,
 }
 
 
-// L2 prefetch, one line per thread, of what the critical path of the coming
-// phases reads from global memory besides flag words: the next layer's ln_1,
-// ln_2 and QKV bias (ln_f as well at the last layer), and this CTA's rows of
-// the KV cache for the attention phase (rows before pos, written by earlier
-// steps).  With HBM saturated by the weight stream, a demand miss on these
-// would cost several microseconds on the critical path.
 // Every layer's norm weights and QKV bias (and ln_f), spread over the grid, into L2 as evict-last
 // lines at the start of a launch: together a few hundred KB that every step reads on its critical
 // path, and that a demand miss would fetch from an HBM saturated by the weight stream.
@@ -534,6 +528,12 @@ __device__ void prefetch_small_vectors(const DecodeArgs& a, const Smem& s, int t
         }
     }
 }
+// L2 prefetch, one line per thread, of what the critical path of the coming
+// phases reads from global memory besides flag words: the next layer's ln_1,
+// ln_2 and QKV bias (ln_f as well at the last layer), and this CTA's rows of
+// the KV cache for the attention phase (rows before pos, written by earlier
+// steps).  With HBM saturated by the weight stream, a demand miss on these
+// would cost several microseconds on the critical path.
 __device__ void prefetch_norms(const DecodeArgs& a, const Smem& s, int l, int tid) {
     const LayerPtrs& N = s.layers[l + 1 < a.NL ? l + 1 : 0];
     if (tid < 32) prefetch_l2_keep(N.ln1 + tid * 64);
