@@ -552,22 +552,30 @@ int num_sms() {
     return n > 0 ? n : 148;
 }
 
-// Split plan: rows per split (a multiple of the tile).  Items (head, split)
-// are spread over a persistent grid of one CTA per SM, so the plan aims at a
-// whole number of items per CTA with at most ~32 tiles (1 MB) per item.
+// Split plan: rows per split (a multiple of the 64-row tile).  Items (head, split) are dealt to a
+// persistent grid of one CTA per SM round-robin (item i to CTA i % sms), so a call lasts as long as
+// its busiest CTA: ceil(items / sms) items of `tps` tiles each (the last split of a head may be
+// shorter).  The plan minimises that CTA's tiles plus half a tile per item (its query load and
+// partial write), and among equal plans takes the smaller split count (fewer partials to merge).
+// E.g. 16 heads x 16384 rows on 148 SMs: 9 splits of 29 tiles, one item per CTA, where splitting
+// into 10 would give 12 CTAs two items of 26 tiles.
 void plan(int L, int H, int* S, int* rows) {
     const int tiles = (L + kFdRows - 1) / kFdRows;
-    const int sms = num_sms();
-    const long long total = (long long)tiles * H;
-    long long per_cta = (total + sms - 1) / sms;  // tiles per CTA if perfectly balanced
-    long long items_per_cta = (per_cta + 31) / 32;
-    if (items_per_cta < 1) items_per_cta = 1;
-    int s = (int)((items_per_cta * sms + H - 1) / H);
-    if (s > tiles) s = tiles;
-    if (s > kFdMergeMax) s = kFdMergeMax;
-    if (s < 1) s = 1;
-    const int tps = (tiles + s - 1) / s;
-    *rows = tps * kFdRows;
+    const long long sms = num_sms();
+    const int smax = std::min(tiles, kFdMergeMax);
+    long long best = -1;
+    int best_tps = tiles;
+    for (int s = 1; s <= smax; ++s) {
+        const int tps = (tiles + s - 1) / s;
+        const int sa = (tiles + tps - 1) / tps;  // splits actually needed with tps tiles each
+        if (sa != s) continue;                   // the same plan as a smaller s
+        const long long load = ((long long)sa * H + sms - 1) / sms * (2LL * tps + 1);  // in half tiles
+        if (best < 0 || load < best) {
+            best = load;
+            best_tps = tps;
+        }
+    }
+    *rows = best_tps * kFdRows;
     *S = (L + *rows - 1) / *rows;
 }
 
