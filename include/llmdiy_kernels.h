@@ -107,6 +107,13 @@ int llmdiy_p2p_close(void* peer_ptr);
 int llmdiy_p2p_free(void* ptr);
 int llmdiy_fd_p2p_merge(const float* part, const uint64_t* peers, int world, int rank, int num_heads, uint32_t tag,
                         uint16_t* O, int* err, void* stream);
+/* The shard's partials and the exchange in two launches (no counterpart in the reference): the split
+ * kernel of llmdiy_fd_mh_partials over this rank's L rows, then llmdiy_fd_p2p_merge's kernel, which
+ * merges each head's split partials itself before pushing them (no separate merge launch).  `work`
+ * as for llmdiy_fd_mh_partials; the other arguments as for llmdiy_fd_p2p_merge. */
+int llmdiy_fd_mh_p2p(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride, int num_heads,
+                     float* work, size_t work_bytes, const uint64_t* peers, int world, int rank, uint32_t tag,
+                     uint16_t* O, int* err, void* stream);
 
 /* No counterpart in the reference.  Split-KV flash decoding of one head in a single launch that
  * allocates nothing: the same result, bit for bit, as llmdiy_fd_v5_split_stage1 + llmdiy_fd_opt_stage2

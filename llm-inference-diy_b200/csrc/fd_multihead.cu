@@ -473,23 +473,29 @@ constexpr uint32_t kP2pPollLimit = 1u << 20;  // about a second of polling
 
 __host__ __device__ inline size_t p2p_region_floats(int world, int H) { return (size_t)world * H * (kFdPart + 1); }
 
-__global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __restrict__ part,
+// `part` holds S partials per head ([H][S][130]): the CTA first merges its head's S into one (S = 1:
+// already merged, the merge is then exact), which is what it pushes.
+__global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __restrict__ part, int S,
                                                              const unsigned long long* __restrict__ peers, int world,
                                                              int rank, int H, uint32_t tag, half* __restrict__ O,
                                                              int* err) {
     __shared__ float scratch[8 * kFdPart];
     __shared__ float red[4];
+    __shared__ float mine[kFdPart];
     const int h = blockIdx.x, d = threadIdx.x;
     const size_t region = (tag & 1u) * p2p_region_floats(world, H);  // floats before this call's region
     const size_t flag_off = region + (size_t)world * H * kFdPart;   // floats before its flags
-    const float* src = part + (size_t)h * kFdPart;
+    fd_merge_head(part + (size_t)h * S * kFdPart, S, kFdPart, scratch, 8 * kFdPart, red, nullptr, mine);
+    __syncthreads();
+    const float* src = mine;
     for (int p = 0; p < world; ++p) {
         float* dst = reinterpret_cast<float*>(peers[p]) + region + ((size_t)rank * H + h) * kFdPart;
         for (int i = d; i < kFdPart; i += kFdHeadDim) dst[i] = src[i];
     }
-    __syncthreads();  // every thread's stores are issued before thread 0's fence
+    __syncthreads();  // every thread's stores precede thread 0's flag stores
     if (d == 0) {
-        __threadfence_system();  // the partial is visible at every rank before its flag
+        // st.release.sys: the CTA's partial (ordered before this thread by the barrier) is visible
+        // at a rank before the flag that announces it
         for (int p = 0; p < world; ++p) {
             unsigned int* f = reinterpret_cast<unsigned int*>(reinterpret_cast<float*>(peers[p]) + flag_off);
             asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f + (size_t)rank * H + h), "r"(tag) : "memory");
@@ -590,8 +596,9 @@ int check_args(const void* Q, const void* K, const void* V, int L, int stride, i
 // before first use; a kernel only ever sets it, llmdiy_fd_mh_status reads and clears it).
 size_t work_floats(int H, int S) { return (size_t)H * S * kFdPart + 4; }
 
-int launch_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride, int H, float* work,
-                    int S, int rows, uint16_t* O, float* out_part, cudaStream_t st) {
+// The persistent split kernel alone: per-split partials [H][S][130] in `work`.
+int launch_split_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride, int H,
+                          float* work, int S, int rows, cudaStream_t st) {
     CUtensorMap tk, tv;
     if (!make_map(&tk, K, L, stride) || !make_map(&tv, V, L, stride)) return (int)cudaErrorInvalidValue;
     int* err = reinterpret_cast<int*>(work + (size_t)H * S * kFdPart);  // set by the kernel, cleared by the status query
@@ -604,7 +611,13 @@ int launch_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int
     fd_partials_k<<<grid, kFdThreads, sizeof(FdSmem), st>>>(tk, tv, reinterpret_cast<const half*>(Q), L, S, H, rows,
                                                              work, err);
     e = cudaGetLastError();
-    if (e != cudaSuccess) return (int)e;
+    return (int)e;
+}
+
+int launch_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride, int H, float* work,
+                    int S, int rows, uint16_t* O, float* out_part, cudaStream_t st) {
+    const int rc = launch_split_partials(Q, K, V, L, stride, H, work, S, rows, st);
+    if (rc) return rc;
     fd_merge_splits_k<<<H, kFdMergeThreads, 0, st>>>(work, S, reinterpret_cast<half*>(O), out_part);
     return (int)cudaGetLastError();
 }
@@ -720,7 +733,25 @@ extern "C" int llmdiy_fd_p2p_merge(const float* part, const uint64_t* peers, int
         num_heads <= 0 || tag == 0)
         return (int)cudaErrorInvalidValue;
     fd_p2p_merge_k<<<num_heads, kFdHeadDim, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        part, reinterpret_cast<const unsigned long long*>(peers), world, rank, num_heads, tag,
+        part, 1, reinterpret_cast<const unsigned long long*>(peers), world, rank, num_heads, tag,
         reinterpret_cast<half*>(O), err);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int llmdiy_fd_mh_p2p(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride,
+                                int num_heads, float* work, size_t work_bytes, const uint64_t* peers, int world,
+                                int rank, uint32_t tag, uint16_t* O, int* err, void* stream) {
+    int rc = check_args(Q, K, V, L, stride, num_heads);
+    if (rc) return rc;
+    if (!peers || !O || !err || world <= 0 || world > kFdMergeMax || rank < 0 || rank >= world || tag == 0)
+        return (int)cudaErrorInvalidValue;
+    int S, rows;
+    plan(L, num_heads, &S, &rows);
+    if (!work || work_bytes < work_floats(num_heads, S) * sizeof(float)) return (int)cudaErrorInvalidValue;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    rc = launch_split_partials(Q, K, V, L, stride, num_heads, work, S, rows, st);
+    if (rc) return rc;
+    fd_p2p_merge_k<<<num_heads, kFdHeadDim, 0, st>>>(work, S, reinterpret_cast<const unsigned long long*>(peers),
+                                                     world, rank, num_heads, tag, reinterpret_cast<half*>(O), err);
     return (int)cudaGetLastError();
 }

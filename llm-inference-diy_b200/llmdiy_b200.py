@@ -84,6 +84,7 @@ def lib() -> ctypes.CDLL:
         "llmdiy_p2p_close": [P],
         "llmdiy_p2p_free": [P],
         "llmdiy_fd_p2p_merge": [P, P, I, I, I, ctypes.c_uint32, P, P, P],
+        "llmdiy_fd_mh_p2p": [P, P, P, I, I, I, P, SZ, P, I, I, ctypes.c_uint32, P, P, P],
         "llmdiy_argmax": [P, P, I, P],
         "llmdiy_hgemv": [P, P, P, I, I, P],
         "llmdiy_hgemm_swizzle_nn": [P, P, P, I, I, I, P],
@@ -267,6 +268,12 @@ def p2p_free(ptr):
 def fd_p2p_merge(part, peers, world, rank, num_heads, tag, O, err, stream=None):
     _check(lib().llmdiy_fd_p2p_merge(_p(part), _p(peers), world, rank, num_heads, tag, _p(O), _p(err), _p(stream)),
            "fd_p2p_merge")
+
+
+def fd_mh_p2p(Q, K, V, L, stride, num_heads, work, work_bytes, peers, world, rank, tag, O, err, stream=None):
+    """This rank's split partials over its L rows, then the peer exchange and merge (two launches)."""
+    _check(lib().llmdiy_fd_mh_p2p(_p(Q), _p(K), _p(V), L, stride, num_heads, _p(work), work_bytes, _p(peers), world,
+                                  rank, tag, _p(O), _p(err), _p(stream)), "fd_mh_p2p")
 
 
 def argmax(out, logits, V, stream=None):

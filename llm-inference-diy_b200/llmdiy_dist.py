@@ -81,6 +81,15 @@ class P2PExchange:
         L.fd_p2p_merge(part.data_ptr(), self.peers.data_ptr(), self.world, self.rank, self.num_heads, self.tag,
                        out.data_ptr(), self.err.data_ptr(), stream=stream)
 
+    def shard(self, q, K, V, rows, stride, work, out, stream):
+        """This rank's split partials over its `rows` cached rows and the exchange, in two launches
+        (llmdiy_fd_mh_p2p: the exchange kernel merges the head's split partials itself)."""
+        import llmdiy_b200 as L
+        self.tag += 1
+        L.fd_mh_p2p(q.data_ptr(), K.data_ptr(), V.data_ptr(), rows, stride, self.num_heads, work.data_ptr(),
+                    work.numel() * 4, self.peers.data_ptr(), self.world, self.rank, self.tag, out.data_ptr(),
+                    self.err.data_ptr(), stream=stream)
+
     def status(self) -> int:
         """0, or 1 when a wait for another rank's flags expired (after synchronising)."""
         return int(self.err.item())
@@ -134,12 +143,19 @@ class SplitKVAttention:
             self._bufs = (torch.empty((self.num_heads, PART), dtype=torch.float32, device=q.device),
                           torch.empty((self.world, self.num_heads, PART), dtype=torch.float32, device=q.device))
         part, parts = self._bufs
-        self._partials(q, K_shard, V_shard, r1 - r0, part)
         if self.exchange == "p2p":
             if self._p2p is None:
                 self._p2p = P2PExchange(self.group, self.num_heads, q.device)
-            self._p2p(part, out, torch.cuda.current_stream(q.device).cuda_stream)
+            st = torch.cuda.current_stream(q.device).cuda_stream
+            if self._partials == self._gpu_partials and r1 > r0:
+                # the split kernel then the exchange kernel, which merges the splits itself
+                self._p2p.shard(q, K_shard, V_shard, r1 - r0, self.stride, self._workspace(r1 - r0, q.device), out,
+                                st)
+            else:
+                self._partials(q, K_shard, V_shard, r1 - r0, part)
+                self._p2p(part, out, st)
             return out
+        self._partials(q, K_shard, V_shard, r1 - r0, part)
         gather_partials(self.group, part, self.world, parts)
         self._merge(parts, out)
         return out
@@ -148,6 +164,15 @@ class SplitKVAttention:
         if self._p2p is not None:
             self._p2p.close()
             self._p2p = None
+
+    def _workspace(self, rows, device):
+        """The split kernel's workspace for `rows` rows (zero-filled once: its error word)."""
+        import torch
+        import llmdiy_b200 as L
+        nb = L.fd_mh_work_bytes(rows, self.num_heads)
+        if self._work is None or self._work.numel() * 4 < nb:
+            self._work = torch.zeros((nb + 3) // 4, dtype=torch.float32, device=device)
+        return self._work
 
     # ---- default implementations: the sm_100a kernels
     def _gpu_partials(self, q, K, V, rows, part):
@@ -158,9 +183,8 @@ class SplitKVAttention:
             part.zero_()
             part[:, 128] = float("-inf")
             return
+        self._workspace(rows, q.device)
         nb = L.fd_mh_work_bytes(rows, self.num_heads)
-        if self._work is None or self._work.numel() * 4 < nb:
-            self._work = torch.zeros((nb + 3) // 4, dtype=torch.float32, device=q.device)
         st = torch.cuda.current_stream(q.device).cuda_stream
         L.fd_mh_partials(q.data_ptr(), K.data_ptr(), V.data_ptr(), rows, self.stride, self.num_heads,
                          part.data_ptr(), self._work.data_ptr(), nb, stream=st)

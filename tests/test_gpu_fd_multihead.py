@@ -196,3 +196,28 @@ def test_fd_p2p_wait_expires_without_a_peer():
     finally:
         L.p2p_free(own)
         L.p2p_free(other)
+
+
+def test_fd_mh_p2p_single_rank(oracle, rng):
+    """The one-call shard path (llmdiy_fd_mh_p2p through SplitKVAttention with the peer exchange):
+    the split kernel, then the exchange kernel merging each head's splits itself, one rank on one GPU,
+    against the oracle; two calls in a row (both buffer regions)."""
+    import llmdiy_dist as D
+    t = torch()
+    H, stride, n = 16, 2048, 5000
+    att = D.SplitKVAttention(None, H, stride, exchange="p2p")
+    try:
+        for call in range(2):
+            q, K, V = _inputs(rng, n, H, stride)
+            dq, dK, dV = dev(q), dev(K), dev(V)
+            O = zeros16(H * 128)
+            att(dq, dK, dV, n, O)
+            t.cuda.synchronize()
+            assert att._p2p.status() == 0
+            assert L.fd_mh_status(att._work.data_ptr(), n, H) == 0
+            got = host(O).reshape(H, 128)
+            for h in (0, 5, H - 1):
+                exp = oracle.attention_q1(q[h * 128:(h + 1) * 128], K[h * 128:], V[h * 128:], n, stride)
+                assert max_abs(got[h], exp) < 1e-3, (call, h)
+    finally:
+        att.close()
