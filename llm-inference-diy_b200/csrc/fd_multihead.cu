@@ -13,10 +13,11 @@
 // before the final merge of the shards' partials.
 //
 // Short caches (L <= 2048 rows) take a single launch instead: one thread-block
-// cluster of 8 CTAs per head (fd_cluster_k), each CTA loading its share of the
-// head's rows in 64-row TMA tiles at once and reducing them to a partial, then
-// CTA 0 of the cluster merging the 8 partials through distributed shared
-// memory.  No global scratch, no memset, no second kernel.
+// cluster of 8 CTAs per head (fd_cluster_k), each CTA reading its share of the
+// head's rows with 16-byte loads straight into registers (sixteen in flight per
+// lane) and reducing them to a partial, then CTA 0 of the cluster merging the 8
+// partials through distributed shared memory.  No global scratch, no memset, no
+// second kernel.
 #include <cooperative_groups.h>
 #include <cuda.h>
 #include <algorithm>
@@ -231,32 +232,26 @@ __global__ void __launch_bounds__(kFdThreads, 1)
 }
 
 // ------------------------------------------------------------------ short caches: one cluster per head
-constexpr int kFcCluster = 8;                                     // CTAs per head (portable cluster size)
-constexpr int kFcMaxTiles = 4;                                    // 64-row tiles per CTA
-constexpr int kFcMaxRows = kFcCluster * kFcMaxTiles * kFdRows;    // 2048 rows per head at most
+constexpr int kFcCluster = 8;        // CTAs per head (portable cluster size)
+constexpr int kFcMaxRows = 2048;     // rows per head at most (256 per CTA)
 constexpr int kFcThreads = 256;
 
-// Shared memory: this header, then the CTA's T K tiles and T V tiles (T = R / 64, sized at launch so
-// that short caches leave room for more CTAs per SM).
-struct __align__(1024) FcSmem {
-    uint64_t full[kFcMaxTiles];
+struct FcSmem {
     float so[kFcThreads / 32][kFdHeadDim];
     float sm[kFcThreads / 32], sl[kFcThreads / 32];
     float po[kFdHeadDim];  // this CTA's partial: o (unnormalised), then m and l
     float pm, pl;
 };
-constexpr size_t kFcHeader = (sizeof(FcSmem) + 1023) / 1024 * 1024;
 
-// Cluster h (CTAs 8h .. 8h+7) attends head h; CTA rank r takes rows [r R, min(L, (r+1) R)), R a
-// multiple of 64.  All of its tiles are requested at once (one mbarrier each); warp w folds rows
-// w*8 .. w*8+7 of every tile (half-warp hw the rows of parity hw, 16-byte loads, online softmax),
-// then the CTA merges its 8 warps into a partial in shared memory.  After a cluster barrier, CTA 0
-// reads the 8 partials over distributed shared memory and writes the head's fp16 output; a second
-// barrier keeps every CTA's shared memory alive until then.  A copy wait that expires sets *err
-// (never cleared by the kernel) and the CTA still takes part in both barriers.
+// Cluster h (CTAs 8h .. 8h+7) attends head h; CTA rank r takes rows [r R, min(L, (r+1) R)).  Each
+// half-warp folds every 16th row into its online softmax (16-byte loads, a lane holds 8 of the 128
+// dims), then the CTA merges its 8 warps into a partial in shared memory.  After a cluster barrier,
+// CTA 0 reads the 8 partials over distributed shared memory and writes the head's fp16 output; a
+// second barrier keeps every CTA's shared memory alive until then.  The kernel has no waits of its
+// own besides the two cluster barriers, which every CTA reaches.
 __global__ void __cluster_dims__(kFcCluster, 1, 1) __launch_bounds__(kFcThreads, 1)
-    fd_cluster_k(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
-                 const half* __restrict__ Q, int L, int R, half* __restrict__ O, int* err) {
+    fd_cluster_k(const half* __restrict__ Kp, const half* __restrict__ Vp, int stride,
+                 const half* __restrict__ Q, int L, int R, half* __restrict__ O) {
     namespace cg = cooperative_groups;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     FcSmem& s = *reinterpret_cast<FcSmem*>(smem_raw);
@@ -264,47 +259,36 @@ __global__ void __cluster_dims__(kFcCluster, 1, 1) __launch_bounds__(kFcThreads,
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, hw = lane >> 4, dl = (lane & 15) * 8;
     const int rank = (int)cluster.block_rank(), h = blockIdx.x / kFcCluster;
     const int r0 = rank * R, r1 = min(L, r0 + R);
-    const int T = r1 > r0 ? (r1 - r0 + kFdRows - 1) / kFdRows : 0;
-    half* ktiles = reinterpret_cast<half*>(smem_raw + kFcHeader);           // [R/64][64 * 128]
-    half* vtiles = ktiles + (size_t)(R / kFdRows) * kFdRows * kFdHeadDim;  // [R/64][64 * 128]
-    if (tid == 0) {
-        for (int t = 0; t < T; ++t) mbar_init(&s.full[t], 1);
-        mbar_fence_init();
-    }
-    __syncthreads();
-    if (tid == 0) {
-        const uint64_t pol = l2_policy_evict_first();
-        for (int t = 0; t < T; ++t) {
-            mbar_arrive_expect_tx(&s.full[t], 2 * kFdTileBytes);
-            tma_load_2d_hint(ktiles + t * kFdRows * kFdHeadDim, &tk, h * kFdHeadDim, r0 + t * kFdRows, &s.full[t],
-                             pol);
-            tma_load_2d_hint(vtiles + t * kFdRows * kFdHeadDim, &tv, h * kFdHeadDim, r0 + t * kFdRows, &s.full[t],
-                             pol);
-        }
-    }
+    // direct 16-byte loads, no staging: half-warp q (of 16) takes rows r0 + q, r0 + q + 16, ...,
+    // eight at a time with all sixteen loads of a batch in flight
+    const int hq = warp * 2 + hw;
     float q8[8];
     unpack8(*reinterpret_cast<const uint4*>(Q + (size_t)h * kFdHeadDim + dl), q8);
     const float scale = __frcp_rn(sqrtf((float)kFdHeadDim));
     float m = -INFINITY, l = 0.f, o8[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) o8[e] = 0.f;
-    bool failed = false;
-    for (int t = 0; t < T; ++t) {
-        if (__syncthreads_or(!mbar_wait(&s.full[t], 0))) {
-            failed = true;
-            break;
-        }
-        const half* kt = ktiles + t * kFdRows * kFdHeadDim;
-        const half* vt = vtiles + t * kFdRows * kFdHeadDim;
-        const int nvalid = min(kFdRows, r1 - (r0 + t * kFdRows));
-        float sc[4];
-        uint4 vr[4];
+    const half* Kh = reinterpret_cast<const half*>(Kp) + (size_t)h * kFdHeadDim + dl;
+    const half* Vh = reinterpret_cast<const half*>(Vp) + (size_t)h * kFdHeadDim + dl;
+    // the loop bound is CTA-uniform (every lane iterates together: the q.k sums shuffle across the
+    // half-warp); rows past r1 are masked
+    for (int base = r0; base < r1; base += 8 * 16) {
+        const int b0 = base + hq;
+        uint4 kr[8], vr[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int r = warp * 8 + 2 * j + hw;
+        for (int j = 0; j < 8; ++j) {
+            const int r = b0 + 16 * j;
+            kr[j] = vr[j] = make_uint4(0u, 0u, 0u, 0u);
+            if (r < r1) {
+                kr[j] = __ldcs(reinterpret_cast<const uint4*>(Kh + (size_t)r * stride));
+                vr[j] = __ldcs(reinterpret_cast<const uint4*>(Vh + (size_t)r * stride));
+            }
+        }
+        float sc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
             float kf[8];
-            unpack8(*reinterpret_cast<const uint4*>(kt + r * kFdHeadDim + dl), kf);
-            vr[j] = *reinterpret_cast<const uint4*>(vt + r * kFdHeadDim + dl);
+            unpack8(kr[j], kf);
             float d = 0.f;
 #pragma unroll
             for (int e = 0; e < 8; ++e) d = __fmaf_rn(q8[e], kf[e], d);
@@ -313,11 +297,11 @@ __global__ void __cluster_dims__(kFcCluster, 1, 1) __launch_bounds__(kFcThreads,
 #pragma unroll
         for (int mk = 8; mk >= 1; mk >>= 1)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], mk);
+            for (int j = 0; j < 8; ++j) sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], mk);
         float mx = m;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            sc[j] = warp * 8 + 2 * j + hw < nvalid ? sc[j] * scale : -INFINITY;
+        for (int j = 0; j < 8; ++j) {
+            sc[j] = b0 + 16 * j < r1 ? sc[j] * scale : -INFINITY;
             mx = fmaxf(mx, sc[j]);
         }
         if (mx != -INFINITY) {
@@ -326,7 +310,7 @@ __global__ void __cluster_dims__(kFcCluster, 1, 1) __launch_bounds__(kFcThreads,
 #pragma unroll
             for (int e = 0; e < 8; ++e) o8[e] *= corr;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < 8; ++j) {
                 const float p = __expf(sc[j] - mx);
                 l += p;
                 float vf[8];
@@ -380,10 +364,6 @@ __global__ void __cluster_dims__(kFcCluster, 1, 1) __launch_bounds__(kFcThreads,
         O[(size_t)h * kFdHeadDim + tid] = f2h(acc * __frcp_rn(Ls));
     }
     cluster.sync();  // CTA 0 has read every peer's partial
-    if (failed && tid == 0) {
-        atomicExch(err, 1);
-        for (int t = 0; t < T; ++t) (void)mbar_wait(&s.full[t], 0);  // copies in flight land here first
-    }
 }
 
 // Merge of a head's S split partials (part = [H][S][130]) with 256 threads:
@@ -622,23 +602,14 @@ int launch_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int
     return (int)cudaGetLastError();
 }
 
-// Short caches: one launch of fd_cluster_k, H clusters of 8 CTAs.  The error word (the workspace's
-// word after the partials) is only ever set by the kernels; the status query clears it.
-int launch_cluster(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride, int H, float* work,
-                   int S, uint16_t* O, cudaStream_t st) {
-    CUtensorMap tk, tv;
-    if (!make_map(&tk, K, L, stride) || !make_map(&tv, V, L, stride)) return (int)cudaErrorInvalidValue;
-    int* err = reinterpret_cast<int*>(work + (size_t)H * S * kFdPart);
-    static std::once_flag attr;
-    std::call_once(attr, [] {
-        cudaFuncSetAttribute(fd_cluster_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(kFcHeader + 2 * kFcMaxTiles * kFdTileBytes));
-    });
-    const int per = (L + kFcCluster - 1) / kFcCluster;
-    const int R = (per + kFdRows - 1) / kFdRows * kFdRows;
-    const size_t smem = kFcHeader + 2 * (size_t)(R / kFdRows) * kFdTileBytes;
-    fd_cluster_k<<<H * kFcCluster, kFcThreads, smem, st>>>(tk, tv, reinterpret_cast<const half*>(Q), L, R,
-                                                            reinterpret_cast<half*>(O), err);
+// Short caches: one launch of fd_cluster_k, H clusters of 8 CTAs (no bounded waits, so the
+// workspace's error word is left as it is).
+int launch_cluster(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride, int H,
+                   uint16_t* O, cudaStream_t st) {
+    const int per = (L + kFcCluster - 1) / kFcCluster;  // rows per CTA
+    fd_cluster_k<<<H * kFcCluster, kFcThreads, sizeof(FcSmem), st>>>(
+        reinterpret_cast<const half*>(K), reinterpret_cast<const half*>(V), stride, reinterpret_cast<const half*>(Q),
+        L, per, reinterpret_cast<half*>(O));
     return (int)cudaGetLastError();
 }
 
@@ -659,7 +630,7 @@ extern "C" int llmdiy_fd_multihead(const uint16_t* Q, const uint16_t* K, const u
     plan(L, num_heads, &S, &rows);
     if (!O || !work || work_bytes < work_floats(num_heads, S) * sizeof(float)) return (int)cudaErrorInvalidValue;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (L <= kFcMaxRows) return launch_cluster(Q, K, V, L, stride, num_heads, work, S, O, st);
+    if (L <= kFcMaxRows) return launch_cluster(Q, K, V, L, stride, num_heads, O, st);
     return launch_partials(Q, K, V, L, stride, num_heads, work, S, rows, O, nullptr, st);
 }
 
