@@ -231,20 +231,22 @@ def test_reference_engine_stream(small_bin, engine):
 
 
 def test_chunked_prefill_matches_oracle():
-    """A prompt longer than the prefill's 2048-row chunk: the second chunk attends over the first
-    chunk's cached rows.  KV rows of the last layer across the chunk boundary against the oracle."""
+    """A prompt longer than the prefill's 2048-row chunk: the second chunk (700 rows at positions
+    2048..2747, six q tiles of 34 to 44 key tiles each) attends over the first chunk's cached rows.
+    KV rows of the last layer, which depend on the first layer's attention, against the oracle
+    across both chunks."""
     import oracle as orc
-    cfg = dict(SMALL, max_seqlen=2200)
+    cfg = dict(SMALL, max_seqlen=2800)
     d = tempfile.mkdtemp()
     p = os.path.join(d, "chunk.bin")
     L.write_random_bin(p, L.make_config(**cfg), seed=SEED + 1)
     e = L.Engine(p)
     m = orc.OracleModel(p, nthreads=os.cpu_count() or 8)
     rng = np.random.default_rng(21)
-    prompt = rng.integers(0, cfg["vocab_size"], 2100).tolist()
+    prompt = rng.integers(0, cfg["vocab_size"], 2748).tolist()
     e.prefill(prompt)
     m.prefill(prompt)
-    for lo, n in ((0, 16), (2040, 60)):
+    for lo, n in ((0, 16), (1000, 64), (1900, 148), (2040, 60), (2300, 64), (2680, 68)):
         k, v = e.kv(1, lo, n)
         ok_, ov = m.kv(1, lo, n)
         assert float(np.max(np.abs(k.astype(np.float32) - ok_.astype(np.float32)))) < 2e-2, lo
