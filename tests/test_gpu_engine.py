@@ -186,9 +186,31 @@ def test_driver_protocol(small_bin, engine):
     assert "invalid token id" in p.stderr
 
 
-def test_driver_batch_verb(small_bin, engine):
+def _oracle_stream_agrees(omodel, prompt, got):
+    """The oracle's greedy stream for `prompt` against `got`: equal, or first different at a step
+    where the oracle's logits of its token and of ours are at most one fp16 ulp apart (a near tie).
+    Returns the number of equal leading tokens."""
+    from gpu_util import f16_ulp
+    omodel.reset()
+    ref = omodel.generate(prompt, len(got), stop_on_eos=False)
+    first = next((i for i, (a, b) in enumerate(zip(got, ref)) if a != b), len(got))
+    if first < len(got):
+        omodel.reset()
+        omodel.prefill(prompt[:-1])
+        tok, pos = prompt[-1], len(prompt) - 1
+        for i in range(first + 1):
+            o, lg, _ = omodel.step(tok, pos, want_logits=True)
+            tok, pos = o, pos + 1
+        margin = float(lg[o]) - float(lg[got[first]])
+        assert margin <= float(f16_ulp(lg[o])), (prompt, first, got, ref, margin)
+    return first
+
+
+def test_driver_batch_verb(small_bin, engine, omodel):
     """The driver's "batch" verb (continuous batching, two slots for six requests): every request
-    gets its own turn's tokens, a malformed request is rejected, and plain turns still work after."""
+    gets its own turn's tokens, each request's stream equals the CPU oracle's greedy stream for its
+    prompt (or first differs at a near tie), a malformed request is rejected, and plain turns still
+    work after."""
     env = dict(os.environ, LLMDIY_MAX_NEW_TOKENS="12", LLMDIY_IGNORE_EOS="1", LLMDIY_MAX_BATCH="2",
                LLMDIY_BATCH_MAX_LEN="256")
     prompts = [[5, 6, 7, 8], [9], [100, 200, 300], [11, 12], [1, 2, 3, 4, 5, 6, 7], [40, 41]]
@@ -207,10 +229,9 @@ def test_driver_batch_verb(small_bin, engine):
             got[r].append(t)
     assert sorted(done) == list(range(7))
     for r, q in enumerate(prompts):
-        want = engine.generate(q, 12, stop_on_eos=False)
         assert len(got[r]) == 12, (r, got[r])
-        n_same = next((i for i, (a, b) in enumerate(zip(got[r], want)) if a != b), 12)
-        assert n_same >= 8, (r, got[r], want)  # batched GEMMs vs the GEMV decode: same greedy stream
+        n_same = _oracle_stream_agrees(omodel, q, got[r])
+        print(f"batch request {r}: {n_same} of 12 tokens equal to the oracle's stream")
     assert got[6] == [] and "invalid token id" in p.stderr
     turns = _parse_turns("\n".join(out[i1 + 1:]))
     assert turns == [engine.generate([5, 6, 7, 8], 12, stop_on_eos=False)]
