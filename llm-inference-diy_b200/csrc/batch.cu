@@ -362,6 +362,65 @@ __global__ void __launch_bounds__(256) splitk_reduce_k(const float* __restrict__
     if (live && part == 0) epi(row, n, v);
 }
 
+// The residual GEMMs (o_proj, c_proj: N = kHidden) followed by the next RMSNorm in one launch:
+// block r sums row r's split-K slices in slice order (splitk_reduce_k's arithmetic), adds them to
+// the residual row as EpiResidual does, and normalises the new row with weight w as
+// rmsnorm_rows_k does (thread t owns columns 8t .. 8t + 7), so x and xn are bit-identical to the
+// reduce + RMSNorm pair.  256 threads, one block per row.
+constexpr int kResNormBatch = 8;  // slices in flight per thread
+
+__global__ void __launch_bounds__(256) splitk_residual_norm_k(const float* __restrict__ ws, int Z, int M,
+                                                              half* __restrict__ x, half* __restrict__ xn,
+                                                              const half* __restrict__ w) {
+    __shared__ float red[17];
+    const int r = blockIdx.x, t = threadIdx.x;
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * t);  // weights: no dependence on earlier kernels
+    pdl_wait();
+    pdl_launch_dependents();
+    const float* src = ws + (size_t)r * kHidden + 8 * t;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int z0 = 0; z0 < Z; z0 += kResNormBatch) {
+        float4 f[2 * kResNormBatch];
+#pragma unroll
+        for (int z = 0; z < kResNormBatch; ++z) {
+            if (z0 + z < Z) {
+                const float* p = src + (size_t)(z0 + z) * M * kHidden;
+                f[2 * z] = *reinterpret_cast<const float4*>(p);
+                f[2 * z + 1] = *reinterpret_cast<const float4*>(p + 4);
+            }
+        }
+#pragma unroll
+        for (int z = 0; z < kResNormBatch; ++z) {
+            if (z0 + z < Z) {
+                acc[0] += f[2 * z].x;
+                acc[1] += f[2 * z].y;
+                acc[2] += f[2 * z].z;
+                acc[3] += f[2 * z].w;
+                acc[4] += f[2 * z + 1].x;
+                acc[5] += f[2 * z + 1].y;
+                acc[6] += f[2 * z + 1].z;
+                acc[7] += f[2 * z + 1].w;
+            }
+        }
+    }
+    half* px = x + (size_t)r * kHidden + 8 * t;
+    float xf[8], of[8];
+    unpack8(*reinterpret_cast<const uint4*>(px), xf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) of[e] = xf[e] + h2f(f2h(acc[e]));
+    const uint4 v = pack8(of);
+    *reinterpret_cast<uint4*>(px) = v;
+    const float sc = rms_scale_regs2048(v, 1e-6f, red, t, 1);
+    float wf[8];
+    unpack8(v, xf);
+    unpack8(wv, wf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) of[e] = (xf[e] * sc) * wf[e];
+    *reinterpret_cast<uint4*>(xn + (size_t)r * kHidden + 8 * t) = pack8(of);
+}
+
 // ---------------------------------------------------------------- ragged split-KV attention
 // Work items are (sequence b, head h, split sp) over rows [sp*S, min(len, (sp+1)*S)), S = kBSplitRows.
 // Longest first: every full split (S / 64 tiles) is numbered before the partial last
@@ -701,6 +760,7 @@ struct llmdiy_batch {
     bool wrows = false;  // weight-row GEMMs (env LLMDIY_BATCH_WROWS=1) instead of split-K + reduce
     int wr_fit[kWrMaxSplit + 1] = {};  // clusters of each size the weight-row GEMM fits at once
     bool pdl = true;  // step kernels launched with programmatic dependent launch (env LLMDIY_BATCH_PDL=0: off)
+    bool fused_norm = true;  // residual GEMMs' slice sums fused with the next RMSNorm (env LLMDIY_BATCH_FUSED_NORM=0: off)
     int hist_steps = 0;
     half* pf = nullptr;  // prefill scratch (kPrefillChunk rows)
     std::vector<CUtensorMap> kmaps, vmaps;  // per layer, over [max_batch * max_len][H]
@@ -843,6 +903,23 @@ int gemm_rows(llmdiy_batch* b, const half* A, int lda, const half* W, int N, int
                             N, epi);
 }
 
+// x += A W^T (N = kHidden), then xn = RMSNorm(x) with weight w: split-K slices + one
+// splitk_residual_norm_k launch, or (weight-row GEMMs, a single slice, or
+// LLMDIY_BATCH_FUSED_NORM=0) the GEMM with the residual epilogue and rmsnorm_rows_k.
+int gemm_residual_norm(llmdiy_batch* b, const half* A, int lda, const half* W, int K, int M, const half* w,
+                       cudaStream_t st) {
+    const int z = ksplit_for(kHidden, K, b->v.num_sms);
+    if (b->fused_norm && !b->wrows && z > 1 && (size_t)z * M * kHidden <= b->ws_floats) {
+        int rc = launch_gemm_tc(A, lda, W, K, M, kHidden, K, EpiPartial{b->ws, M, kHidden}, st, z, b->pdl);
+        if (rc) return rc;
+        return (int)launch_step(b->pdl, splitk_residual_norm_k, dim3(M), dim3(256), 0, st, (const float*)b->ws, z, M,
+                                b->x, b->xn, w);
+    }
+    int rc = gemm_rows(b, A, lda, W, kHidden, K, M, EpiResidual{b->x}, st);
+    if (rc) return rc;
+    return (int)launch_step(b->pdl, rmsnorm_rows_k, dim3(M), dim3(256), 0, st, b->xn, (const half*)b->x, w);
+}
+
 // One greedy step for sequences 0..B-1 (tok, pos on the device), enqueued on st.
 int enqueue_step(llmdiy_batch* b, int B, cudaStream_t st) {
     const EngineView& v = b->v;
@@ -851,11 +928,13 @@ int enqueue_step(llmdiy_batch* b, int B, cudaStream_t st) {
     cudaError_t ce = cudaMemsetAsync(b->ctr, 0, sizeof(int) * NL, st);
     if (ce != cudaSuccess) return (int)ce;
     embed_rows_k<<<B, 256, 0, st>>>(v.wte, b->tok, b->x);  // after the memset: stream order
+    BCK0(launch_step(b->pdl, rmsnorm_rows_k, dim3(B), dim3(256), 0, st, b->xn, (const half*)b->x, v.layers[0].ln1));
     for (int l = 0; l < NL; ++l) {
         const LayerPtrs& L = v.layers[l];
         half* kcl = b->kc + (size_t)l * b->layer_stride;
         half* vcl = b->vc + (size_t)l * b->layer_stride;
-        BCK0(launch_step(b->pdl, rmsnorm_rows_k, dim3(B), dim3(256), 0, st, b->xn, (const half*)b->x, L.ln1));
+        // xn holds RMSNorm(x) with this layer's ln_1 weight (before the loop, or from the last
+        // layer's c_proj step)
         int rc = gemm_rows(b, b->xn, kHidden, L.qkv_w, 3 * kHidden, kHidden, B,
                            EpiQKVRows{L.qkv_b, b->q, kcl, vcl, b->pos, b->max_len}, st);
         if (rc) return rc;
@@ -864,15 +943,13 @@ int enqueue_step(llmdiy_batch* b, int B, cudaStream_t st) {
                          b->ctr + l, b->err));
         BCK0(launch_step(b->pdl, bfd_merge_k, dim3(B * kHeads), dim3(kHeadDim), 0, st, (const float*)b->fdp,
                          (const int*)b->pos, b->Smax, b->att));
-        rc = gemm_rows(b, b->att, kHidden, L.proj_w, kHidden, kHidden, B, EpiResidual{b->x}, st);
+        rc = gemm_residual_norm(b, b->att, kHidden, L.proj_w, kHidden, B, L.ln2, st);
         if (rc) return rc;
-        BCK0(launch_step(b->pdl, rmsnorm_rows_k, dim3(B), dim3(256), 0, st, b->xn, (const half*)b->x, L.ln2));
         rc = gemm_rows(b, b->xn, kHidden, L.w12, 2 * IM, kHidden, B, EpiSwiGLU{b->act, IM}, st);
         if (rc) return rc;
-        rc = gemm_rows(b, b->act, IM, L.cproj, kHidden, IM, B, EpiResidual{b->x}, st);
+        rc = gemm_residual_norm(b, b->act, IM, L.cproj, IM, B, l + 1 < NL ? v.layers[l + 1].ln1 : v.lnf, st);
         if (rc) return rc;
     }
-    BCK0(launch_step(b->pdl, rmsnorm_rows_k, dim3(B), dim3(256), 0, st, b->xn, (const half*)b->x, v.lnf));
     int rc = gemm_rows(b, b->xn, kHidden, v.lm_head, V, kHidden, B, EpiStoreRows{b->logits, V}, st);
     if (rc) return rc;
     BCK0(launch_step(b->pdl, argmax_rows_k, dim3(B), dim3(1024), 0, st, b->next, (const half*)b->logits, V));
@@ -901,6 +978,7 @@ int llmdiy_batch_create(llmdiy_engine* e, int max_batch, int max_len, llmdiy_bat
     b->max_len = max_len;
     if (const char* wr = std::getenv("LLMDIY_BATCH_WROWS")) b->wrows = wr[0] == '1';
     if (const char* pd = std::getenv("LLMDIY_BATCH_PDL")) b->pdl = pd[0] != '0';
+    if (const char* fn = std::getenv("LLMDIY_BATCH_FUSED_NORM")) b->fused_norm = fn[0] != '0';
     b->Smax = (max_len + kBSplitRows - 1) / kBSplitRows;
     const size_t H = kHidden, IM = c.intermediate_size, V = c.vocab_size, NL = c.num_layers;
     b->layer_stride = (size_t)max_batch * max_len * H;

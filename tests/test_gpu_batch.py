@@ -148,3 +148,26 @@ def test_batch_overlapped_launch_matches_serial(engine, monkeypatch):
         b.close()
     assert np.array_equal(out["0"][0], out["1"][0])
     assert np.array_equal(out["0"][1], out["1"][1])
+
+
+@pytest.mark.parametrize("B", [5, 64])
+def test_batch_fused_residual_norm_matches_separate(engine, monkeypatch, B):
+    """o_proj and c_proj slice sums fused with the following RMSNorm (the default: one launch that
+    sums the split-K slices of a row in slice order, adds the residual and normalises the row)
+    against the reduce kernel + RMSNorm kernel pair (LLMDIY_BATCH_FUSED_NORM=0): the same arithmetic
+    in the same order, so identical tokens and logits bit for bit over several steps."""
+    rng = np.random.default_rng(67 + B)
+    steps = 4
+    lens = rng.integers(1, 600, B).tolist()
+    toks = rng.integers(0, SMALL["vocab_size"], B).tolist()
+    out = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("LLMDIY_BATCH_FUSED_NORM", mode)
+        b = L.Batch(engine, max_batch=B, max_len=620)
+        for s in range(B):
+            b.fill_random(s, lens[s], seed=800 + s)
+        t = b.decode(toks, lens, steps)
+        out[mode] = (t, np.stack([b.logits(s).view(np.uint16) for s in range(B)]))
+        b.close()
+    assert np.array_equal(out["0"][0], out["1"][0])
+    assert np.array_equal(out["0"][1], out["1"][1])
