@@ -91,15 +91,16 @@ int llmdiy_fd_mh_status(const float* work, int L, int num_heads);
 /* Multi-GPU exchange of the shards' partials over peer memory (no counterpart in the reference,
  * which has no multi-GPU path; replaces an all-gather + llmdiy_fd_mh_merge).  Every rank owns a
  * receive buffer of llmdiy_p2p_buffer_bytes(world, num_heads) bytes (two regions, used by calls of odd
- * and even tag, each [world][num_heads][130] fp32 partials then [world][num_heads] u32 flags, so a rank
- * may start the next call while a slower rank still merges the last one), allocated with
- * llmdiy_p2p_alloc, whose CUDA IPC
- * handle (64 bytes) the other ranks open with llmdiy_p2p_open.  llmdiy_fd_p2p_merge, called by every
- * rank with the same tag (a call counter starting at 1), stores this rank's [num_heads][130] partial
+ * and even tag, each [world][num_heads][130] 8-byte words: an fp32 value in the low half, the call's
+ * tag in the high half; so a rank may start the next call while a slower rank still merges the last
+ * one), allocated with llmdiy_p2p_alloc (zero-filled), whose CUDA IPC handle (64 bytes) the other
+ * ranks open with llmdiy_p2p_open.  llmdiy_fd_p2p_merge, called by every rank with the same tag (a
+ * call counter starting at 1, never 0), stores this rank's [num_heads][130] partial as tagged words
  * into slot `rank` of every rank's buffer (peers[] = device array of the world buffer pointers in rank
- * order, this rank's own included), raises its flags there, waits (bounded) for every rank's flags in
- * its own buffer, and merges the partials in rank order into O.  *err (device int) becomes 1 when a
- * wait expired.  The ranks' kernels must run on different GPUs. */
+ * order, this rank's own included; one 8-byte store per value, no fence), waits (bounded) until every
+ * rank's words in its own buffer carry the tag, and merges the partials in rank order into O.
+ * world <= 16.  *err (device int) becomes 1 when a wait expired.  The ranks' kernels must run on
+ * different GPUs. */
 size_t llmdiy_p2p_buffer_bytes(int world, int num_heads);
 int llmdiy_p2p_alloc(size_t bytes, void** ptr, uint8_t* ipc_handle /* 64 bytes out */);
 int llmdiy_p2p_open(const uint8_t* ipc_handle /* 64 bytes */, void** ptr);

@@ -440,18 +440,21 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_merge_ranks_k(const float* __re
 }
 
 // Exchange + merge over peer memory (one CTA per head): push this rank's partial of head h into
-// slot `rank` of every rank's buffer, publish a flag per (rank, head) after a system-scope fence,
-// wait for every rank's flag in the own buffer, then merge the world's partials in rank order.
+// slot `rank` of every rank's buffer as flag-carrying 8-byte words (the fp32 value in the low half,
+// the call's tag in the high half, one single-copy-atomic store each: no fence and no separate
+// flag), poll the world's words of head h in the own buffer until every one carries the tag, then
+// merge the world's partials in rank order.
 //
-// Each buffer holds two regions, [2] x {partials [world][H][130] fp32, flags [world][H] u32}, and
-// call `tag` uses region (tag & 1).  A rank that has finished call t saw every rank's call-t flags,
-// and a rank raises those only after its own call t-1 kernel (same stream) has finished merging; so
-// the earliest next write into a region, call t+1's, lands after every reader of call t-1 in that
-// region is done, while call t's region may still be read.  One region would let a fast rank's
-// call t+1 overwrite a slot that a slower rank's call t merge is still reading.
+// Each buffer holds two regions of [world][H][130] words, and call `tag` uses region (tag & 1).  A
+// rank that has finished call t saw every rank's call-t words, and a rank writes those only after
+// its own call t-1 kernel (same stream) has finished merging; so the earliest next write into a
+// region, call t+1's, lands after every reader of call t-1 in that region is done, while call t's
+// region may still be read.  One region would let a fast rank's call t+1 overwrite a slot that a
+// slower rank's call t merge is still reading.
 constexpr uint32_t kP2pPollLimit = 1u << 20;  // about a second of polling
+constexpr int kP2pMaxWorld = 16;              // ranks one exchange merges (shared-memory staging)
 
-__host__ __device__ inline size_t p2p_region_floats(int world, int H) { return (size_t)world * H * (kFdPart + 1); }
+__host__ __device__ inline size_t p2p_region_words(int world, int H) { return (size_t)world * H * kFdPart; }
 
 // `part` holds S partials per head ([H][S][130]): the CTA first merges its head's S into one (S = 1:
 // already merged, the merge is then exact), which is what it pushes.
@@ -459,46 +462,67 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __rest
                                                              const unsigned long long* __restrict__ peers, int world,
                                                              int rank, int H, uint32_t tag, half* __restrict__ O,
                                                              int* err) {
-    __shared__ float scratch[8 * kFdPart];
+    __shared__ float scratch[kP2pMaxWorld * kFdPart];
     __shared__ float red[4];
     __shared__ float mine[kFdPart];
-    const int h = blockIdx.x, d = threadIdx.x;
-    const size_t region = (tag & 1u) * p2p_region_floats(world, H);  // floats before this call's region
-    const size_t flag_off = region + (size_t)world * H * kFdPart;   // floats before its flags
+    const int h = blockIdx.x, d = threadIdx.x, lane = d & 31, warp = d >> 5;
+    const size_t region = (tag & 1u) * p2p_region_words(world, H);  // words before this call's region
     fd_merge_head(part + (size_t)h * S * kFdPart, S, kFdPart, scratch, 8 * kFdPart, red, nullptr, mine);
     __syncthreads();
-    const float* src = mine;
+    const unsigned long long hi = (unsigned long long)tag << 32;
     for (int p = 0; p < world; ++p) {
-        float* dst = reinterpret_cast<float*>(peers[p]) + region + ((size_t)rank * H + h) * kFdPart;
-        for (int i = d; i < kFdPart; i += kFdHeadDim) dst[i] = src[i];
-    }
-    __syncthreads();  // every thread's stores precede thread 0's flag stores
-    if (d == 0) {
-        // st.release.sys: the CTA's partial (ordered before this thread by the barrier) is visible
-        // at a rank before the flag that announces it
-        for (int p = 0; p < world; ++p) {
-            unsigned int* f = reinterpret_cast<unsigned int*>(reinterpret_cast<float*>(peers[p]) + flag_off);
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f + (size_t)rank * H + h), "r"(tag) : "memory");
+        unsigned long long* dst = reinterpret_cast<unsigned long long*>(peers[p]) + region + ((size_t)rank * H + h) * kFdPart;
+        for (int i = d; i < kFdPart; i += kFdHeadDim) {
+            const unsigned long long w = hi | __float_as_uint(mine[i]);
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + i), "l"(w) : "memory");
         }
     }
-    const float* own = reinterpret_cast<const float*>(peers[rank]) + region;  // this call's region here
+    // every word of head h from every rank, polled in the own buffer: thread d takes element d of
+    // each rank (and threads 0, 1 elements 128, 129)
+    const unsigned long long* own = reinterpret_cast<const unsigned long long*>(peers[rank]) + region;
+    const int per = d < kFdPart - kFdHeadDim ? 2 : 1;
+    uint32_t pending = world * per >= 32 ? 0xffffffffu : (1u << (world * per)) - 1u;  // bit j * per + k: rank j, element d + 128 k
     bool ok = true;
-    if (d < world) {
-        const unsigned int* f = reinterpret_cast<const unsigned int*>(own + (size_t)world * H * kFdPart) + d * H + h;
-        ok = false;
-        for (uint32_t i = 0; i < kP2pPollLimit; ++i) {
-            unsigned int v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-            if (v == tag) { ok = true; break; }
-            if (i > 64) __nanosleep(64);
+    for (uint32_t it = 0; pending && it < kP2pPollLimit; ++it) {
+        for (int j = 0; j < world; ++j) {
+            for (int k = 0; k < per; ++k) {
+                const uint32_t bit = 1u << (j * per + k);
+                if (!(pending & bit)) continue;
+                const int e = d + k * kFdHeadDim;
+                unsigned long long w;
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];"
+                             : "=l"(w)
+                             : "l"(own + ((size_t)j * H + h) * kFdPart + e)
+                             : "memory");
+                if ((uint32_t)(w >> 32) == tag) {
+                    scratch[j * kFdPart + e] = __uint_as_float((uint32_t)w);
+                    pending &= ~bit;
+                }
+            }
         }
+        if (pending && it > 64) __nanosleep(64);
     }
+    ok = pending == 0;
     if (!__syncthreads_and(ok)) {
         if (d == 0) atomicExch(err, 1);
         return;
     }
-    fd_merge_head(own + (size_t)h * kFdPart, world, H * kFdPart, scratch, 8 * kFdPart, red,
-                  O + (size_t)h * kFdHeadDim, nullptr);
+    // merge in rank order (fd_merge_head's arithmetic, from shared memory)
+    float mx = -INFINITY;
+    for (int j = d; j < world; j += kFdHeadDim) mx = fmaxf(mx, scratch[j * kFdPart + kFdHeadDim]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float Ls = 0.f, acc = 0.f;
+    for (int j = 0; j < world; ++j) {
+        const float mj = scratch[j * kFdPart + kFdHeadDim];
+        const float f = mj == -INFINITY ? 0.f : __expf(mj - M);
+        Ls = __fmaf_rn(scratch[j * kFdPart + kFdHeadDim + 1], f, Ls);
+        acc = __fmaf_rn(f, scratch[j * kFdPart + d], acc);
+    }
+    O[(size_t)h * kFdHeadDim + d] = f2h(acc * __frcp_rn(Ls));
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -666,7 +690,7 @@ extern "C" int llmdiy_fd_mh_status(const float* work, int L, int num_heads) {
 
 extern "C" size_t llmdiy_p2p_buffer_bytes(int world, int num_heads) {
     if (world <= 0 || num_heads <= 0) return 0;
-    const size_t b = 2 * p2p_region_floats(world, num_heads) * sizeof(float);  // two regions (tag parity)
+    const size_t b = 2 * p2p_region_words(world, num_heads) * sizeof(unsigned long long);  // two regions (tag parity)
     return (b + 255) / 256 * 256;
 }
 
@@ -700,7 +724,7 @@ extern "C" int llmdiy_p2p_free(void* ptr) { return (int)cudaFree(ptr); }
 
 extern "C" int llmdiy_fd_p2p_merge(const float* part, const uint64_t* peers, int world, int rank, int num_heads,
                                    uint32_t tag, uint16_t* O, int* err, void* stream) {
-    if (!part || !peers || !O || !err || world <= 0 || world > kFdMergeMax || rank < 0 || rank >= world ||
+    if (!part || !peers || !O || !err || world <= 0 || world > kP2pMaxWorld || rank < 0 || rank >= world ||
         num_heads <= 0 || tag == 0)
         return (int)cudaErrorInvalidValue;
     fd_p2p_merge_k<<<num_heads, kFdHeadDim, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
@@ -714,7 +738,7 @@ extern "C" int llmdiy_fd_mh_p2p(const uint16_t* Q, const uint16_t* K, const uint
                                 int rank, uint32_t tag, uint16_t* O, int* err, void* stream) {
     int rc = check_args(Q, K, V, L, stride, num_heads);
     if (rc) return rc;
-    if (!peers || !O || !err || world <= 0 || world > kFdMergeMax || rank < 0 || rank >= world || tag == 0)
+    if (!peers || !O || !err || world <= 0 || world > kP2pMaxWorld || rank < 0 || rank >= world || tag == 0)
         return (int)cudaErrorInvalidValue;
     int S, rows;
     plan(L, num_heads, &S, &rows);

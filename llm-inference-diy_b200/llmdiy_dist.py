@@ -6,7 +6,8 @@ The cache's positions are sharded contiguously over the ranks of a process group
 with llmdiy_fd_mh_partials; then either the partials are all-gathered (NCCL over
 NVLink) and every rank merges them in rank order with llmdiy_fd_mh_merge, or one
 kernel per rank stores its partial straight into every rank's buffer over peer
-memory, raises flags and merges (P2PExchange, llmdiy_fd_p2p_merge).  This is the
+memory as tagged words and merges once every rank's words carry the call's tag
+(P2PExchange, llmdiy_fd_p2p_merge).  This is the
 only exchange on the path: 130 x num_heads fp32 per rank.
 
 The reference has no multi-GPU path; its single-GPU counterpart is the per-head
@@ -46,8 +47,9 @@ def gather_partials(group, part, world: int, out=None):
 class P2PExchange:
     """The partials exchange over peer memory (llmdiy_fd_p2p_merge): every rank allocates a receive
     buffer, the ranks swap its CUDA IPC handle through the process group once, and each call is one
-    kernel per rank that stores the rank's partial into every buffer, raises flags and merges when
-    all ranks' flags are up.  Collective: every rank constructs it and calls it in the same order."""
+    kernel per rank that stores the rank's partial into every buffer as 8-byte words carrying the
+    call's tag and merges when every rank's words in its own buffer carry it.  Up to 16 ranks.
+    Collective: every rank constructs it and calls it in the same order."""
 
     def __init__(self, group, num_heads: int, device):
         import torch
@@ -91,7 +93,7 @@ class P2PExchange:
                     self.err.data_ptr(), stream=stream)
 
     def status(self) -> int:
-        """0, or 1 when a wait for another rank's flags expired (after synchronising)."""
+        """0, or 1 when a wait for another rank's words expired (after synchronising)."""
         return int(self.err.item())
 
     def close(self):

@@ -123,20 +123,24 @@ def test_fd_multihead_rejects_bad_arguments(rng):
 
 def test_fd_p2p_exchange_single_rank(oracle, rng):
     """The peer-memory exchange kernel (llmdiy_fd_p2p_merge) with one rank on one GPU: the partial
-    goes through the rank's own IPC-exported buffer and flag, and the merge equals the attention
-    over the shard; later calls (new tags) reuse the buffer.  The multi-rank run is the 2-GPU
-    `bench.py --workload fd-op`, which checks it against the NCCL all-gather path."""
+    goes through the rank's own IPC-exported buffer as tagged 8-byte words, and the merge equals the
+    attention over the shard; later calls (new tags) reuse the buffer.  The multi-rank run is the
+    2-GPU `bench.py --workload fd-op`, which checks it against the NCCL all-gather path."""
     import llmdiy_dist as D
     t = torch()
     H, stride, n = 16, 2048, 3000
     ex = D.P2PExchange(None, H, t.device("cuda"))
 
-    class _View:  # the exchange's own receive buffer as a float32 tensor (no copy)
+    class _View:  # the exchange's own receive buffer as an int64 tensor of its words (no copy)
         def __init__(self, ptr, n):
-            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 2}
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i8", "data": (ptr, False), "version": 2}
 
-    region = H * 131  # floats per region: [1][H][130] partials + [1][H] flags
-    buf = t.as_tensor(_View(ex.own, 2 * region), device="cuda")
+    region = H * 130  # words per region: [1][H][130], value in the low half, tag in the high half
+    words = t.as_tensor(_View(ex.own, 2 * region), device="cuda")
+
+    def region_values(r):  # (values [H][130] as float32, tags [H][130])
+        w = words[r * region:(r + 1) * region]
+        return ((w & 0xFFFFFFFF).to(t.int32).view(t.float32).view(H, 130), (w >> 32).view(H, 130))
     parts = []
     try:
         for call in range(3):
@@ -156,20 +160,20 @@ def test_fd_p2p_exchange_single_rank(oracle, rng):
                 assert max_abs(got[h], exp) < 1e-3, (call, h)
             # call `tag` writes region (tag & 1); the other region keeps the previous call's partial
             parts.append(part.clone())
-            r = (call + 1) & 1
-            assert t.equal(buf[r * region: r * region + H * 130].view(H, 130), part)
+            vals, tags = region_values((call + 1) & 1)
+            assert t.equal(vals, part) and bool((tags == call + 1).all())
             if call:
-                r0 = call & 1
-                assert t.equal(buf[r0 * region: r0 * region + H * 130].view(H, 130), parts[call - 1])
+                vals, tags = region_values(call & 1)
+                assert t.equal(vals, parts[call - 1]) and bool((tags == call).all())
     finally:
         ex.close()
 
 
 def test_fd_p2p_wait_expires_without_a_peer():
     """Failure detection without a GPU fault: a rank of a two-rank exchange whose peer never runs.
-    The partner's buffer is a second local buffer that nothing writes flags into, so the kernel's
-    bounded wait for rank 1 runs out; the kernel reports it in the error word and returns, and the
-    context stays usable for a normal call afterwards."""
+    The partner's buffer is a second local buffer, and nothing writes rank 1's tagged words into this
+    rank's buffer, so the kernel's bounded wait for them runs out; the kernel reports it in the error
+    word and returns, and the context stays usable for a normal call afterwards."""
     import time
     t = torch()
     H = 16
