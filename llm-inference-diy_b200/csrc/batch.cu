@@ -14,8 +14,11 @@
 // GEMMs are the tcgen05 kernel; with M = B <= 64 rows a GEMM has few output
 // tiles, so the K dimension is split over grid.z until the tiles x slices
 // fill the SMs, and a reduce kernel sums the fp32 slices in order and applies
-// the epilogue op (deterministic).  A step is captured once in a CUDA graph;
-// llmdiy_batch_decode replays it per step.
+// the epilogue op (deterministic; for o_proj and c_proj the same launch also
+// applies the next RMSNorm).  The attention runs two persistent CTAs per SM,
+// each with its own three-stage TMA pipeline, claiming work items from a
+// counter.  A step is captured once in a CUDA graph; llmdiy_batch_decode
+// replays it per step.
 //
 // Cache layout per layer: [max_batch][max_len][H] fp16 (row r of sequence b of
 // layer l at ((l * max_batch + b) * max_len + r) * H), the engine's row format.
@@ -42,7 +45,8 @@ namespace {
 constexpr int kBatchMax = 64;
 constexpr int kBRows = 64;   // KV rows per TMA tile
 constexpr int kBSplitRows = 4096;  // KV rows per attention work item (each boundary costs a partial write)
-constexpr int kBStages = 6;
+constexpr int kBStages = 3;       // K/V tiles in flight per CTA; two CTAs share an SM (6 per SM)
+constexpr int kBCtasPerSm = 2;    // two independent pipelines per SM stream faster than one twice as deep
 constexpr int kBPart = kHeadDim + 2;
 
 // ---------------------------------------------------------------- GEMM epilogues
@@ -472,7 +476,7 @@ __device__ __forceinline__ void bfd_item(const BFdSmem& s, int item, int B, BIte
 
 // Each item writes the unnormalised partial (o[128], m, l) of its rows to
 // part[((b*16 + h) * Smax + sp) * 130]; bfd_merge_k combines a sequence's splits.
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(128, kBCtasPerSm)
     bfd_partials_k(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                    const half* __restrict__ q, const int* __restrict__ pos, int B, int max_len, int Smax,
                    float* __restrict__ part, int* ctr, int* err) {
@@ -938,9 +942,9 @@ int enqueue_step(llmdiy_batch* b, int B, cudaStream_t st) {
         int rc = gemm_rows(b, b->xn, kHidden, L.qkv_w, 3 * kHidden, kHidden, B,
                            EpiQKVRows{L.qkv_b, b->q, kcl, vcl, b->pos, b->max_len}, st);
         if (rc) return rc;
-        BCK0(launch_step(b->pdl, bfd_partials_k, dim3(v.num_sms), dim3(128), sizeof(BFdSmem), st, b->kmaps[l],
-                         b->vmaps[l], (const half*)b->q, (const int*)b->pos, B, b->max_len, b->Smax, b->fdp,
-                         b->ctr + l, b->err));
+        BCK0(launch_step(b->pdl, bfd_partials_k, dim3(kBCtasPerSm * v.num_sms), dim3(128), sizeof(BFdSmem), st,
+                         b->kmaps[l], b->vmaps[l], (const half*)b->q, (const int*)b->pos, B, b->max_len, b->Smax,
+                         b->fdp, b->ctr + l, b->err));
         BCK0(launch_step(b->pdl, bfd_merge_k, dim3(B * kHeads), dim3(kHeadDim), 0, st, (const float*)b->fdp,
                          (const int*)b->pos, b->Smax, b->att));
         rc = gemm_residual_norm(b, b->att, kHidden, L.proj_w, kHidden, B, L.ln2, st);
