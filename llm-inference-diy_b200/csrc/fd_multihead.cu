@@ -454,6 +454,7 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_merge_ranks_k(const float* __re
 // slower rank's call t merge is still reading.
 constexpr uint32_t kP2pPollLimit = 1u << 20;  // about a second of polling
 constexpr int kP2pMaxWorld = 16;              // ranks one exchange merges (shared-memory staging)
+constexpr int kP2pStage = 40;                 // partials staged per pass (the split merge: one pass up to 40 splits)
 
 __host__ __device__ inline size_t p2p_region_words(int world, int H) { return (size_t)world * H * kFdPart; }
 
@@ -463,12 +464,13 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __rest
                                                              const unsigned long long* __restrict__ peers, int world,
                                                              int rank, int H, uint32_t tag, half* __restrict__ O,
                                                              int* err) {
-    __shared__ float scratch[kP2pMaxWorld * kFdPart];
+    static_assert(kP2pStage >= kP2pMaxWorld, "the rank merge stages every rank at once");
+    __shared__ float scratch[kP2pStage * kFdPart];
     __shared__ float red[4];
     __shared__ float mine[kFdPart];
     const int h = blockIdx.x, d = threadIdx.x, lane = d & 31, warp = d >> 5;
     const size_t region = (tag & 1u) * p2p_region_words(world, H);  // words before this call's region
-    fd_merge_head(part + (size_t)h * S * kFdPart, S, kFdPart, scratch, 8 * kFdPart, red, nullptr, mine);
+    fd_merge_head(part + (size_t)h * S * kFdPart, S, kFdPart, scratch, kP2pStage * kFdPart, red, nullptr, mine);
     __syncthreads();
     const unsigned long long hi = (unsigned long long)tag << 32;
     for (int p = 0; p < world; ++p) {
