@@ -90,6 +90,105 @@ __device__ __forceinline__ void fd_merge_head(const float* p, int n, int jstride
     }
 }
 
+// Exchange + merge over peer memory (one CTA per head): push this rank's partial of head h into
+// slot `rank` of every rank's buffer as flag-carrying 8-byte words (the fp32 value in the low half,
+// the call's tag in the high half, one single-copy-atomic store each: no fence and no separate
+// flag), poll the world's words of head h in the own buffer until every one carries the tag, then
+// merge the world's partials in rank order.
+//
+// Each buffer holds two regions of [world][H][130] words, and call `tag` uses region (tag & 1).  A
+// rank that has finished call t saw every rank's call-t words, and a rank writes those only after
+// its own call t-1 kernel (same stream) has finished merging; so the earliest next write into a
+// region, call t+1's, lands after every reader of call t-1 in that region is done, while call t's
+// region may still be read.  One region would let a fast rank's call t+1 overwrite a slot that a
+// slower rank's call t merge is still reading.
+constexpr uint32_t kP2pPollLimit = 1u << 20;  // about a second of polling
+constexpr int kP2pMaxWorld = 16;              // ranks one exchange merges (shared-memory staging)
+constexpr int kP2pStage = 40;                 // partials staged per pass (the split merge: one pass up to 40 splits)
+
+__host__ __device__ inline size_t p2p_region_words(int world, int H) { return (size_t)world * H * kFdPart; }
+
+// One head's exchange by the 128 threads of a CTA (a CTA-uniform call): merge the head's S split
+// partials (part_h = [S][130]; S = 1: already merged, the merge is then exact), push the result as
+// tagged words into slot `rank` of every rank's buffer, wait (bounded) until every rank's words of
+// head h in the own buffer carry the tag, and merge them in rank order into O[h].  scratch holds
+// `cap` >= kP2pMaxWorld * 130 floats.  Returns false (and sets *err) when the wait expired.
+__device__ bool exchange_head(const float* part_h, int S, const unsigned long long* __restrict__ peers, int world,
+                              int rank, int H, int h, uint32_t tag, half* __restrict__ O, int* err, float* scratch,
+                              int cap, float* red, float* mine) {
+    const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+    const size_t region = (tag & 1u) * p2p_region_words(world, H);  // words before this call's region
+    fd_merge_head(part_h, S, kFdPart, scratch, cap, red, nullptr, mine);
+    __syncthreads();
+    const unsigned long long hi = (unsigned long long)tag << 32;
+    for (int p = 0; p < world; ++p) {
+        unsigned long long* dst = reinterpret_cast<unsigned long long*>(peers[p]) + region + ((size_t)rank * H + h) * kFdPart;
+        for (int i = d; i < kFdPart; i += kFdHeadDim) {
+            const unsigned long long w = hi | __float_as_uint(mine[i]);
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + i), "l"(w) : "memory");
+        }
+    }
+    // every word of head h from every rank, polled in the own buffer: thread d takes element d of
+    // each rank (and threads 0, 1 elements 128, 129)
+    const unsigned long long* own = reinterpret_cast<const unsigned long long*>(peers[rank]) + region;
+    const int per = d < kFdPart - kFdHeadDim ? 2 : 1;
+    uint32_t pending = world * per >= 32 ? 0xffffffffu : (1u << (world * per)) - 1u;  // bit j * per + k: rank j, element d + 128 k
+    for (uint32_t it = 0; pending && it < kP2pPollLimit; ++it) {
+        for (int j = 0; j < world; ++j) {
+            for (int k = 0; k < per; ++k) {
+                const uint32_t bit = 1u << (j * per + k);
+                if (!(pending & bit)) continue;
+                const int e = d + k * kFdHeadDim;
+                unsigned long long w;
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];"
+                             : "=l"(w)
+                             : "l"(own + ((size_t)j * H + h) * kFdPart + e)
+                             : "memory");
+                if ((uint32_t)(w >> 32) == tag) {
+                    scratch[j * kFdPart + e] = __uint_as_float((uint32_t)w);
+                    pending &= ~bit;
+                }
+            }
+        }
+        if (pending && it > 64) __nanosleep(64);
+    }
+    if (!__syncthreads_and(pending == 0)) {
+        if (d == 0) atomicExch(err, 1);
+        return false;
+    }
+    // merge in rank order (fd_merge_head's arithmetic, from shared memory)
+    float mx = -INFINITY;
+    for (int j = d; j < world; j += kFdHeadDim) mx = fmaxf(mx, scratch[j * kFdPart + kFdHeadDim]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float Ls = 0.f, acc = 0.f;
+    for (int j = 0; j < world; ++j) {
+        const float mj = scratch[j * kFdPart + kFdHeadDim];
+        const float f = mj == -INFINITY ? 0.f : __expf(mj - M);
+        Ls = __fmaf_rn(scratch[j * kFdPart + kFdHeadDim + 1], f, Ls);
+        acc = __fmaf_rn(f, scratch[j * kFdPart + d], acc);
+    }
+    O[(size_t)h * kFdHeadDim + d] = f2h(acc * __frcp_rn(Ls));
+    return true;
+}
+
+// The exchange alone, one CTA per head, on partials already in memory ([H][S][130]).
+__global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __restrict__ part, int S,
+                                                             const unsigned long long* __restrict__ peers, int world,
+                                                             int rank, int H, uint32_t tag, half* __restrict__ O,
+                                                             int* err) {
+    static_assert(kP2pStage >= kP2pMaxWorld, "the rank merge stages every rank at once");
+    __shared__ float scratch[kP2pStage * kFdPart];
+    __shared__ float red[4];
+    __shared__ float mine[kFdPart];
+    const int h = blockIdx.x;
+    (void)exchange_head(part + (size_t)h * S * kFdPart, S, peers, world, rank, H, h, tag, O, err, scratch,
+                        kP2pStage * kFdPart, red, mine);
+}
+
 // Persistent: CTA b takes work items (head, split) b, b + grid, ... and its
 // TMA pipeline runs across item boundaries, so the next item's tiles are
 // already in flight when one item ends.  Item i: head i / S, split i % S,
@@ -438,94 +537,6 @@ __global__ void __launch_bounds__(kFdHeadDim) fd_merge_ranks_k(const float* __re
     const int h = blockIdx.x;
     fd_merge_head(parts + (size_t)h * kFdPart, G, H * kFdPart, scratch, 8 * kFdPart, red, O + (size_t)h * kFdHeadDim,
                   nullptr);
-}
-
-// Exchange + merge over peer memory (one CTA per head): push this rank's partial of head h into
-// slot `rank` of every rank's buffer as flag-carrying 8-byte words (the fp32 value in the low half,
-// the call's tag in the high half, one single-copy-atomic store each: no fence and no separate
-// flag), poll the world's words of head h in the own buffer until every one carries the tag, then
-// merge the world's partials in rank order.
-//
-// Each buffer holds two regions of [world][H][130] words, and call `tag` uses region (tag & 1).  A
-// rank that has finished call t saw every rank's call-t words, and a rank writes those only after
-// its own call t-1 kernel (same stream) has finished merging; so the earliest next write into a
-// region, call t+1's, lands after every reader of call t-1 in that region is done, while call t's
-// region may still be read.  One region would let a fast rank's call t+1 overwrite a slot that a
-// slower rank's call t merge is still reading.
-constexpr uint32_t kP2pPollLimit = 1u << 20;  // about a second of polling
-constexpr int kP2pMaxWorld = 16;              // ranks one exchange merges (shared-memory staging)
-constexpr int kP2pStage = 40;                 // partials staged per pass (the split merge: one pass up to 40 splits)
-
-__host__ __device__ inline size_t p2p_region_words(int world, int H) { return (size_t)world * H * kFdPart; }
-
-// `part` holds S partials per head ([H][S][130]): the CTA first merges its head's S into one (S = 1:
-// already merged, the merge is then exact), which is what it pushes.
-__global__ void __launch_bounds__(kFdHeadDim) fd_p2p_merge_k(const float* __restrict__ part, int S,
-                                                             const unsigned long long* __restrict__ peers, int world,
-                                                             int rank, int H, uint32_t tag, half* __restrict__ O,
-                                                             int* err) {
-    static_assert(kP2pStage >= kP2pMaxWorld, "the rank merge stages every rank at once");
-    __shared__ float scratch[kP2pStage * kFdPart];
-    __shared__ float red[4];
-    __shared__ float mine[kFdPart];
-    const int h = blockIdx.x, d = threadIdx.x, lane = d & 31, warp = d >> 5;
-    const size_t region = (tag & 1u) * p2p_region_words(world, H);  // words before this call's region
-    fd_merge_head(part + (size_t)h * S * kFdPart, S, kFdPart, scratch, kP2pStage * kFdPart, red, nullptr, mine);
-    __syncthreads();
-    const unsigned long long hi = (unsigned long long)tag << 32;
-    for (int p = 0; p < world; ++p) {
-        unsigned long long* dst = reinterpret_cast<unsigned long long*>(peers[p]) + region + ((size_t)rank * H + h) * kFdPart;
-        for (int i = d; i < kFdPart; i += kFdHeadDim) {
-            const unsigned long long w = hi | __float_as_uint(mine[i]);
-            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + i), "l"(w) : "memory");
-        }
-    }
-    // every word of head h from every rank, polled in the own buffer: thread d takes element d of
-    // each rank (and threads 0, 1 elements 128, 129)
-    const unsigned long long* own = reinterpret_cast<const unsigned long long*>(peers[rank]) + region;
-    const int per = d < kFdPart - kFdHeadDim ? 2 : 1;
-    uint32_t pending = world * per >= 32 ? 0xffffffffu : (1u << (world * per)) - 1u;  // bit j * per + k: rank j, element d + 128 k
-    bool ok = true;
-    for (uint32_t it = 0; pending && it < kP2pPollLimit; ++it) {
-        for (int j = 0; j < world; ++j) {
-            for (int k = 0; k < per; ++k) {
-                const uint32_t bit = 1u << (j * per + k);
-                if (!(pending & bit)) continue;
-                const int e = d + k * kFdHeadDim;
-                unsigned long long w;
-                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];"
-                             : "=l"(w)
-                             : "l"(own + ((size_t)j * H + h) * kFdPart + e)
-                             : "memory");
-                if ((uint32_t)(w >> 32) == tag) {
-                    scratch[j * kFdPart + e] = __uint_as_float((uint32_t)w);
-                    pending &= ~bit;
-                }
-            }
-        }
-        if (pending && it > 64) __nanosleep(64);
-    }
-    ok = pending == 0;
-    if (!__syncthreads_and(ok)) {
-        if (d == 0) atomicExch(err, 1);
-        return;
-    }
-    // merge in rank order (fd_merge_head's arithmetic, from shared memory)
-    float mx = -INFINITY;
-    for (int j = d; j < world; j += kFdHeadDim) mx = fmaxf(mx, scratch[j * kFdPart + kFdHeadDim]);
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    float Ls = 0.f, acc = 0.f;
-    for (int j = 0; j < world; ++j) {
-        const float mj = scratch[j * kFdPart + kFdHeadDim];
-        const float f = mj == -INFINITY ? 0.f : __expf(mj - M);
-        Ls = __fmaf_rn(scratch[j * kFdPart + kFdHeadDim + 1], f, Ls);
-        acc = __fmaf_rn(f, scratch[j * kFdPart + d], acc);
-    }
-    O[(size_t)h * kFdHeadDim + d] = f2h(acc * __frcp_rn(Ls));
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
