@@ -71,7 +71,8 @@ int llmdiy_gemm_tc_status(void);
  * row r of head h at r*stride + h*128 (stride >= num_heads*128, a multiple of 8); O is [num_heads][128].
  * Scale 1/sqrt(128), fp32 accumulation, fast-math exponentials like the reference.  `work` is caller
  * scratch of llmdiy_fd_mh_work_bytes(L, num_heads) bytes (device memory, 16-byte aligned, zero-filled once
- * before its first use: its last word is the error word, which the kernels only set); nothing is
+ * before its first use: its first word is the error word, which the kernels only set, at the same
+ * place for every L, so a workspace sized for the longest L serves every shorter one); nothing is
  * allocated.  A partial is 130 fp32: o[128] (unnormalised), m (max score), l (sum of e^{s-m}). */
 size_t llmdiy_fd_mh_work_bytes(int L, int num_heads);
 /* O = softmax(q k^T / sqrt(128)) v for every head over rows [0, L).  L <= 2048: one launch, a cluster of

@@ -612,16 +612,19 @@ int check_args(const void* Q, const void* K, const void* V, int L, int stride, i
     return 0;
 }
 
-// Workspace: the split partials [H][S][130] fp32, then one error word (zero-filled by the caller
-// before first use; a kernel only ever sets it, llmdiy_fd_mh_status reads and clears it).
-size_t work_floats(int H, int S) { return (size_t)H * S * kFdPart + 4; }
+// Workspace: a 16-byte control block at the same place for every L (word 0: the error word, which
+// a kernel only ever sets and llmdiy_fd_mh_status reads and clears), then the split partials
+// [H][S][130] fp32.  Zero-filled by the caller before first use; a workspace sized for one L serves
+// every shorter L (the error word does not move with the split count).
+constexpr size_t kFdCtl = 4;  // floats
+size_t work_floats(int H, int S) { return kFdCtl + (size_t)H * S * kFdPart; }
 
 // The persistent split kernel alone: per-split partials [H][S][130] in `work`.
 int launch_split_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int L, int stride, int H,
                           float* work, int S, int rows, cudaStream_t st) {
     CUtensorMap tk, tv;
     if (!make_map(&tk, K, L, stride) || !make_map(&tv, V, L, stride)) return (int)cudaErrorInvalidValue;
-    int* err = reinterpret_cast<int*>(work + (size_t)H * S * kFdPart);  // set by the kernel, cleared by the status query
+    int* err = reinterpret_cast<int*>(work);  // set by the kernel, cleared by the status query
     cudaError_t e;
     static std::once_flag attr;
     std::call_once(attr, [] {
@@ -629,7 +632,7 @@ int launch_split_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* 
     });
     const int grid = std::min(S * H, partials_ctas());
     fd_partials_k<<<grid, kFdThreads, sizeof(FdSmem), st>>>(tk, tv, reinterpret_cast<const half*>(Q), L, S, H, rows,
-                                                             work, err);
+                                                             work + kFdCtl, err);
     e = cudaGetLastError();
     return (int)e;
 }
@@ -638,7 +641,7 @@ int launch_partials(const uint16_t* Q, const uint16_t* K, const uint16_t* V, int
                     int S, int rows, uint16_t* O, float* out_part, cudaStream_t st) {
     const int rc = launch_split_partials(Q, K, V, L, stride, H, work, S, rows, st);
     if (rc) return rc;
-    fd_merge_splits_k<<<H, kFdMergeThreads, 0, st>>>(work, S, reinterpret_cast<half*>(O), out_part);
+    fd_merge_splits_k<<<H, kFdMergeThreads, 0, st>>>(work + kFdCtl, S, reinterpret_cast<half*>(O), out_part);
     return (int)cudaGetLastError();
 }
 
@@ -694,10 +697,8 @@ extern "C" int llmdiy_fd_mh_merge(const float* parts, int G, int num_heads, uint
 
 extern "C" int llmdiy_fd_mh_status(const float* work, int L, int num_heads) {
     if (!work || L <= 0 || num_heads <= 0) return (int)cudaErrorInvalidValue;
-    int S, rows;
-    plan(L, num_heads, &S, &rows);
     int h = 0;
-    int* word = reinterpret_cast<int*>(const_cast<float*>(work) + (size_t)num_heads * S * kFdPart);
+    int* word = reinterpret_cast<int*>(const_cast<float*>(work));  // word 0 for every L
     cudaError_t e = cudaMemcpy(&h, word, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return (int)e;
     if (h) cudaMemset(word, 0, sizeof(int));  // the kernels only ever set it
@@ -762,7 +763,7 @@ extern "C" int llmdiy_fd_mh_p2p(const uint16_t* Q, const uint16_t* K, const uint
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     rc = launch_split_partials(Q, K, V, L, stride, num_heads, work, S, rows, st);
     if (rc) return rc;
-    fd_p2p_merge_k<<<num_heads, kFdHeadDim, 0, st>>>(work, S, reinterpret_cast<const unsigned long long*>(peers),
+    fd_p2p_merge_k<<<num_heads, kFdHeadDim, 0, st>>>(work + kFdCtl, S, reinterpret_cast<const unsigned long long*>(peers),
                                                      world, rank, num_heads, tag, reinterpret_cast<half*>(O), err);
     return (int)cudaGetLastError();
 }

@@ -52,6 +52,25 @@ def test_fd_multihead_vs_oracle(oracle, rng, L_, H, stride):
         assert max_abs(got[h], exp) < 1e-3, h
 
 
+def test_fd_multihead_workspace_reused_across_lengths(oracle, rng):
+    """One workspace sized for the longest cache serves shorter ones: the split kernel's partials of a
+    40000-row call occupy the place where a shorter cache's split count would otherwise have put its
+    error word, and every call still reads back a clean status and the oracle's attention."""
+    t = torch()
+    H, stride = 16, 2048
+    w, nb = _work(40000, H)
+    for n in (40000, 5000, 3000, 40000):
+        q, K, V = _inputs(rng, n, H, stride)
+        dq, dK, dV, O = dev(q), dev(K), dev(V), zeros16(H * 128)
+        L.fd_multihead(dq.data_ptr(), dK.data_ptr(), dV.data_ptr(), O.data_ptr(), n, stride, H, w.data_ptr(), nb)
+        t.cuda.synchronize()
+        assert L.fd_mh_status(w.data_ptr(), n, H) == 0, n
+        got = host(O).reshape(H, 128)
+        for h in (0, H - 1):
+            exp = oracle.attention_q1(q[h * 128:(h + 1) * 128], K[h * 128:], V[h * 128:], n, stride)
+            assert max_abs(got[h], exp) < 1e-3, (n, h)
+
+
 def test_fd_multihead_vs_reference_split(oracle, rng):
     """Config 1 against the reference's split kernels run head by head."""
     ref = ref_kernels()
